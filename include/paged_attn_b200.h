@@ -1,0 +1,222 @@
+/*
+ * paged_attn_b200.h -- C ABI of the B200 (sm_100a) paged-attention library
+ * (libpaged_attn_b200.so).
+ *
+ * The library replaces the paged-attention hot path of
+ * VrajPatel105/paged-inference-engine:
+ *   - kernels/flash_attention.py:19-136   flash_attention_kernel (Triton)
+ *   - kernels/flash_attention.py:139-172  flash_attention_forward (launcher)
+ *   - transformer/model.py:85-122         quantise-on-write of new K/V into the
+ *                                          paged INT8 block cache
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a device pointer unless stated otherwise; strides are in
+ *     ELEMENTS; the innermost (head_dim) stride of every tensor must be 1 and
+ *     every row must start on a 16-byte boundary.
+ *   - The KV pool is addressed as logical [block, slot, head, d] through the
+ *     three strides given, exactly as the reference launcher passes
+ *     K.stride(0), K.stride(2), K.stride(1) to its kernel
+ *     (kernels/flash_attention.py:158-159): for a tensor of shape
+ *     [num_blocks, block_size, num_kv_heads, head_dim] that is
+ *     (stride(0), stride(1), stride(2)).
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Nothing allocates.  Outputs and the split-K workspace are owned by the
+ *     caller.  Work is enqueued asynchronously on `stream`; the return value
+ *     only reports argument / launch errors.  Device-side range problems
+ *     (block ids outside the pool, positions beyond the block table) are
+ *     skipped by the kernels and OR-ed into *status (PA_STATUS_*) when a
+ *     status word is supplied.
+ *   - Return value: PA_OK (0) or a negative PA_ERR_* code;
+ *     paged_attn_error_string() gives the message of the last failing call on
+ *     the calling thread.
+ */
+#ifndef PAGED_ATTN_B200_H
+#define PAGED_ATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. */
+enum {
+  PA_DTYPE_F16 = 0,
+  PA_DTYPE_BF16 = 1,
+  PA_DTYPE_I8 = 2,
+  PA_DTYPE_F32 = 3
+};
+
+/* Return codes. */
+enum {
+  PA_OK = 0,
+  PA_ERR_INVALID = -1,     /* bad argument (shape, stride, alignment, dtype) */
+  PA_ERR_UNSUPPORTED = -2, /* valid but not compiled (e.g. head_dim 96)      */
+  PA_ERR_WORKSPACE = -3,   /* workspace missing or too small                 */
+  PA_ERR_CUDA = -4         /* a CUDA runtime call or launch failed           */
+};
+
+/* Device status bits written through the optional status pointer. */
+enum {
+  PA_STATUS_BAD_BLOCK_ID = 1,
+  PA_STATUS_BAD_POSITION = 2,
+  PA_STATUS_BAD_NUM_BLOCKS = 4,
+  PA_STATUS_BAD_SEQ_INDEX = 8
+};
+
+/*
+ * Paged KV pool.  Replaces the cache buffers of transformer/model.py:62-67
+ * and the K/V/scale arguments of kernels/flash_attention.py:21-33.
+ *   k, v            logical [num_blocks, block_size, num_kv_heads, head_dim]
+ *   dtype           PA_DTYPE_F16, PA_DTYPE_BF16 or PA_DTYPE_I8
+ *   k_scale/v_scale dequantisation scales, required for PA_DTYPE_I8 and
+ *                   ignored otherwise.  Per-(token, head) scales use all three
+ *                   strides; the reference's per-(block, head) scales
+ *                   ([num_blocks, num_kv_heads], kernels/flash_attention.py:73-77)
+ *                   use stride_slot = 0.
+ *   scale_dtype     PA_DTYPE_F16 or PA_DTYPE_F32
+ *   block_size      any power of two
+ */
+typedef struct {
+  void* k;
+  void* v;
+  int32_t dtype;
+  int32_t num_blocks;
+  int32_t block_size;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t scale_dtype;
+  int64_t k_stride_block, k_stride_slot, k_stride_head;
+  int64_t v_stride_block, v_stride_slot, v_stride_head;
+  void* k_scale;
+  void* v_scale;
+  int64_t ks_stride_block, ks_stride_slot, ks_stride_head;
+  int64_t vs_stride_block, vs_stride_slot, vs_stride_head;
+} pa_kv_cache_t;
+
+/*
+ * Per-step paging metadata (kernels/flash_attention.py:27-30, 56-67):
+ *   block_table         int32 [num_seqs, bt_cols], physical block ids
+ *   num_blocks_per_seq  int32 [num_seqs]
+ *   q_len_per_seq       int32 [num_seqs]  query rows of each sequence
+ *   kv_len_per_seq      int32 [num_seqs]  keys of each sequence (incl. the new ones)
+ */
+typedef struct {
+  const int32_t* block_table;
+  int64_t bt_stride_seq, bt_stride_col;
+  int32_t bt_cols;
+  int32_t num_seqs;
+  const int32_t* num_blocks_per_seq;
+  const int32_t* q_len_per_seq;
+  const int32_t* kv_len_per_seq;
+} pa_paging_t;
+
+/*
+ * Attention inputs / outputs (kernels/flash_attention.py:139-150):
+ *   q    [num_seqs, num_q_heads, max_q_len, head_dim], PA_DTYPE_F16 or BF16;
+ *        num_q_heads must be a multiple of num_kv_heads (grouped-query).
+ *   o    fp16, same logical shape as q.  Rows >= q_len_per_seq are not written.
+ *   lse  fp16 [num_seqs, num_q_heads, max_q_len] natural-log log-sum-exp of
+ *        the scaled logits, or NULL.
+ *   softmax_scale   <= 0 selects 1/sqrt(head_dim) (kernels/flash_attention.py:90)
+ *   causal_top_left 0: query row m of a sequence sits at absolute position
+ *        kv_len - q_len + m (correct for decode and chunked prefill);
+ *        1: row m sees keys 0..m, the reference kernel's own mask
+ *        (kernels/flash_attention.py:97), kept for bit-for-bit comparisons.
+ */
+typedef struct {
+  const void* q;
+  int32_t q_dtype;
+  int32_t num_q_heads;
+  int32_t max_q_len;
+  int32_t causal_top_left;
+  int64_t q_stride_seq, q_stride_head, q_stride_row;
+  void* o;
+  int64_t o_stride_seq, o_stride_head, o_stride_row;
+  void* lse;
+  int64_t l_stride_seq, l_stride_head, l_stride_row;
+  float softmax_scale;
+  int32_t _reserved;
+} pa_attn_io_t;
+
+/*
+ * New K/V rows to append (transformer/model.py:76-92):
+ *   k_new, v_new  [num_tokens, num_kv_heads, head_dim], F16 / BF16 / F32
+ *   seq_index     int32 [num_tokens]: block-table row of each token
+ *                 (pos_seq_id in the reference)
+ *   positions     int32 [num_tokens]: absolute position of each token
+ *                 (position_ids in the reference)
+ */
+typedef struct {
+  const void* k_new;
+  const void* v_new;
+  int32_t dtype;
+  int32_t num_tokens;
+  int64_t k_stride_token, k_stride_head;
+  int64_t v_stride_token, v_stride_head;
+  const int32_t* seq_index;
+  const int32_t* positions;
+} pa_kv_new_t;
+
+/*
+ * Bytes of split-K workspace paged_attn_forward / paged_attn_decode need for
+ * this problem on the current device (0 when the prefill kernel is used).
+ */
+int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg,
+                              size_t* bytes);
+
+/*
+ * Paged causal attention forward: replaces flash_attention_forward
+ * (kernels/flash_attention.py:139-172).  Chooses the split-K decode kernel
+ * when max_q_len * (num_q_heads / num_kv_heads) <= 16, else the prefill
+ * kernel.  workspace: >= paged_attn_workspace_size() bytes, 256-byte aligned.
+ */
+int paged_attn_forward(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Split-K (flash-decoding) paged attention for short query blocks: the q_len=1
+ * grid of kernels/flash_attention.py:38-40,153 with grouped-query packing.
+ * Launches the split kernel and its merge kernel on `stream`.
+ */
+int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Tiled causal paged attention for long query blocks (prefill / chunked
+ * prefill): the q_len > 1 grid of kernels/flash_attention.py:19-136.
+ */
+int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                       void* stream);
+
+/*
+ * Quantise-on-write of new K/V rows into an INT8 pool: replaces the per-token
+ * loop of transformer/model.py:85-122 with one scale per (token, kv head):
+ *   absmax = max |x| (fp32), scale = absmax / 127 (fp32; 1.0 when absmax == 0,
+ *   tests/pre_quantize_test.py:6-10), q = clamp(round_half_even(x / scale),
+ *   -127, 127); the scale is stored in the pool's scale dtype.
+ * kv->dtype must be PA_DTYPE_I8 and kv->k_scale / v_scale per-token.
+ */
+int kv_write_quant(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                   void* stream);
+
+/*
+ * Write of new K/V rows into an F16 / BF16 pool (round-to-nearest-even
+ * conversion from the input dtype).  The pool fill of
+ * tests/test_flash_attention.py:33-49 as a scatter through the block table.
+ */
+int kv_write_copy(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                  void* stream);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* paged_attn_error_string(void);
+
+/* Library version, e.g. "0.1.0". */
+const char* paged_attn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_ATTN_B200_H */

@@ -1,0 +1,377 @@
+// extern "C" entry points of libpaged_attn_b200.so (declared in
+// include/paged_attn_b200.h): argument validation, kernel selection and
+// workspace layout.  Nothing here allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "pa_types.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool is_pow2(long long x) { return x > 0 && (x & (x - 1)) == 0; }
+int ilog2(long long x) {
+  int r = 0;
+  while ((1LL << r) < x) ++r;
+  return r;
+}
+bool al(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool row_al(long long stride_elems, int elt, unsigned a) { return ((stride_elems * elt) % a) == 0; }
+
+int elt_size(int dtype) {
+  switch (dtype) {
+    case PA_DTYPE_F16:
+    case PA_DTYPE_BF16:
+      return 2;
+    case PA_DTYPE_I8:
+      return 1;
+    case PA_DTYPE_F32:
+      return 4;
+    default:
+      return 0;
+  }
+}
+
+constexpr int kNcMax = 16;
+constexpr int kMaxDecodeSeqs = 8192;
+
+// Validate a KV pool; fills the pool part of AttnParams / WriteParams.
+int check_cache(const pa_kv_cache_t* kv) {
+  if (!kv) return fail(PA_ERR_INVALID, "kv cache descriptor is NULL");
+  if (kv->dtype != PA_DTYPE_F16 && kv->dtype != PA_DTYPE_BF16 && kv->dtype != PA_DTYPE_I8)
+    return fail(PA_ERR_INVALID, "KV pool dtype %d unsupported (fp16, bf16 or int8)", kv->dtype);
+  if (kv->head_dim != 64 && kv->head_dim != 128)
+    return fail(PA_ERR_UNSUPPORTED, "head_dim %d not compiled (64 or 128)", kv->head_dim);
+  if (!is_pow2(kv->block_size))
+    return fail(PA_ERR_INVALID, "block_size %d must be a power of two", kv->block_size);
+  if (kv->num_kv_heads < 1 || kv->num_blocks < 0) return fail(PA_ERR_INVALID, "bad KV pool shape");
+  if (!kv->k || !kv->v) return fail(PA_ERR_INVALID, "K/V pool pointer is NULL");
+  const int e = elt_size(kv->dtype);
+  if (!al(kv->k, 16) || !al(kv->v, 16)) return fail(PA_ERR_INVALID, "K/V pool must be 16-byte aligned");
+  const long long ks[6] = {kv->k_stride_block, kv->k_stride_slot, kv->k_stride_head,
+                           kv->v_stride_block, kv->v_stride_slot, kv->v_stride_head};
+  for (long long s : ks)
+    if (!row_al(s, e, 16) || s < 0)
+      return fail(PA_ERR_INVALID, "K/V pool strides must be non-negative and keep rows 16-byte aligned");
+  if (kv->dtype == PA_DTYPE_I8) {
+    if (!kv->k_scale || !kv->v_scale) return fail(PA_ERR_INVALID, "int8 KV pool needs k_scale and v_scale");
+    if (kv->scale_dtype != PA_DTYPE_F16 && kv->scale_dtype != PA_DTYPE_F32)
+      return fail(PA_ERR_INVALID, "scale dtype must be fp16 or fp32");
+    const unsigned sa = kv->scale_dtype == PA_DTYPE_F32 ? 4 : 2;
+    if (!al(kv->k_scale, sa) || !al(kv->v_scale, sa)) return fail(PA_ERR_INVALID, "scale tensors misaligned");
+  }
+  return PA_OK;
+}
+
+int check_paging(const pa_paging_t* pg) {
+  if (!pg) return fail(PA_ERR_INVALID, "paging descriptor is NULL");
+  if (pg->num_seqs < 0 || pg->bt_cols < 0) return fail(PA_ERR_INVALID, "negative num_seqs / block table width");
+  if (pg->num_seqs > 0 && (!pg->block_table || !pg->q_len_per_seq || !pg->kv_len_per_seq || !pg->num_blocks_per_seq))
+    return fail(PA_ERR_INVALID, "paging metadata pointer is NULL");
+  return PA_OK;
+}
+
+void fill_cache(pa::AttnParams& p, const pa_kv_cache_t* kv) {
+  p.k = kv->k;
+  p.v = kv->v;
+  p.k_sblk = kv->k_stride_block;
+  p.k_sslot = kv->k_stride_slot;
+  p.k_shead = kv->k_stride_head;
+  p.v_sblk = kv->v_stride_block;
+  p.v_sslot = kv->v_stride_slot;
+  p.v_shead = kv->v_stride_head;
+  p.ks = kv->k_scale;
+  p.vs = kv->v_scale;
+  p.ks_sblk = kv->ks_stride_block;
+  p.ks_sslot = kv->ks_stride_slot;
+  p.ks_shead = kv->ks_stride_head;
+  p.vs_sblk = kv->vs_stride_block;
+  p.vs_sslot = kv->vs_stride_slot;
+  p.vs_shead = kv->vs_stride_head;
+  p.scale_f32 = kv->scale_dtype == PA_DTYPE_F32;
+  p.Hkv = kv->num_kv_heads;
+  p.BS = kv->block_size;
+  p.log2BS = ilog2(kv->block_size);
+  p.NB = kv->num_blocks;
+}
+
+int build_attn(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+               pa::AttnParams& p) {
+  int rc = check_cache(kv);
+  if (rc) return rc;
+  rc = check_paging(pg);
+  if (rc) return rc;
+  if (!io) return fail(PA_ERR_INVALID, "attention io descriptor is NULL");
+  if (io->q_dtype != PA_DTYPE_F16 && io->q_dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_INVALID, "Q dtype must be fp16 or bf16");
+  if (io->num_q_heads < 1 || io->num_q_heads % kv->num_kv_heads)
+    return fail(PA_ERR_INVALID, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                io->num_q_heads, kv->num_kv_heads);
+  if (io->max_q_len < 0) return fail(PA_ERR_INVALID, "max_q_len < 0");
+  if (pg->num_seqs > 0 && io->max_q_len > 0) {
+    if (!io->q || !io->o) return fail(PA_ERR_INVALID, "Q / O pointer is NULL");
+    if (!al(io->q, 16) || !row_al(io->q_stride_seq, 2, 16) || !row_al(io->q_stride_head, 2, 16) ||
+        !row_al(io->q_stride_row, 2, 16))
+      return fail(PA_ERR_INVALID, "Q rows must be 16-byte aligned (contiguous head_dim)");
+    if (!al(io->o, 4) || !row_al(io->o_stride_seq, 2, 4) || !row_al(io->o_stride_head, 2, 4) ||
+        !row_al(io->o_stride_row, 2, 4))
+      return fail(PA_ERR_INVALID, "O rows must be 4-byte aligned");
+    if (io->lse && !al(io->lse, 2)) return fail(PA_ERR_INVALID, "LSE misaligned");
+  }
+  p = pa::AttnParams{};
+  fill_cache(p, kv);
+  p.q = io->q;
+  p.q_sb = io->q_stride_seq;
+  p.q_sh = io->q_stride_head;
+  p.q_sm = io->q_stride_row;
+  p.q_bf16 = io->q_dtype == PA_DTYPE_BF16;
+  p.bt = pg->block_table;
+  p.bt_ss = pg->bt_stride_seq;
+  p.bt_sc = pg->bt_stride_col;
+  p.bt_cols = pg->bt_cols;
+  p.nblk = pg->num_blocks_per_seq;
+  p.qlen = pg->q_len_per_seq;
+  p.kvlen = pg->kv_len_per_seq;
+  p.o = io->o;
+  p.o_sb = io->o_stride_seq;
+  p.o_sh = io->o_stride_head;
+  p.o_sm = io->o_stride_row;
+  p.lse = io->lse;
+  p.l_sb = io->l_stride_seq;
+  p.l_sh = io->l_stride_head;
+  p.l_sm = io->l_stride_row;
+  p.B = pg->num_seqs;
+  p.Hq = io->num_q_heads;
+  p.G = io->num_q_heads / kv->num_kv_heads;
+  p.maxq = io->max_q_len;
+  const float sc = io->softmax_scale > 0.f ? io->softmax_scale : 1.0f / sqrtf(static_cast<float>(kv->head_dim));
+  p.sm_scale = sc;
+  p.scale_log2 = sc * 1.4426950408889634f;
+  p.top_left = io->causal_top_left ? 1 : 0;
+  p.status = status;
+  return PA_OK;
+}
+
+bool use_decode(const pa::AttnParams& p) { return p.maxq * p.G <= kNcMax && p.B <= kMaxDecodeSeqs; }
+int decode_nt(const pa::AttnParams& p) { return p.maxq * p.G <= 8 ? 1 : 2; }
+int kv_kind(int dtype) { return dtype == PA_DTYPE_F16 ? pa::KV_F16 : dtype == PA_DTYPE_BF16 ? pa::KV_BF16 : pa::KV_I8; }
+
+// Persistent decode grid, cached per (device, variant, num_seqs).
+int cached_grid(int kv, int qbf, int D, int nt, int B) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, kv, qbf, D, nt, B);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int g = pa::decode_grid_size(kv, qbf, D, nt, B);
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = g;
+  return g;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct WsLayout {
+  size_t part_o, part_ml, tstart, total;
+};
+WsLayout ws_layout(int warps, int D, int B) {
+  WsLayout l;
+  l.part_o = 0;
+  l.part_ml = align256(static_cast<size_t>(2) * warps * kNcMax * D * sizeof(float));
+  l.tstart = l.part_ml + align256(static_cast<size_t>(2) * warps * kNcMax * 2 * sizeof(float));
+  l.total = l.tstart + align256(static_cast<size_t>(B + 1) * sizeof(int));
+  return l;
+}
+
+int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream) {
+  if (p.B > kMaxDecodeSeqs)
+    return fail(PA_ERR_UNSUPPORTED, "decode kernel supports at most %d sequences per call", kMaxDecodeSeqs);
+  if (p.maxq * p.G > kNcMax)
+    return fail(PA_ERR_UNSUPPORTED, "decode kernel packs at most %d (q rows x group heads) columns", kNcMax);
+  if (p.B == 0 || p.maxq == 0) return PA_OK;
+  const int nt = decode_nt(p);
+  const int kv_k = kv_kind(kv->dtype);
+  const int grid = cached_grid(kv_k, p.q_bf16, kv->head_dim, nt, p.B);
+  if (grid <= 0) return fail(PA_ERR_CUDA, "could not size the decode grid (no CUDA device?)");
+  const int warps = grid * pa::decode_warps_per_cta();
+  const WsLayout L = ws_layout(warps, kv->head_dim, p.B);
+  if (!ws || ws_bytes < L.total)
+    return fail(PA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", L.total, ws_bytes);
+  if (!al(ws, 256)) return fail(PA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  char* base = static_cast<char*>(ws);
+  p.part_o = reinterpret_cast<float*>(base + L.part_o);
+  p.part_ml = reinterpret_cast<float*>(base + L.part_ml);
+  p.tstart = reinterpret_cast<int*>(base + L.tstart);
+  p.num_warps_total = warps;
+  cudaError_t e = pa::launch_decode(p, kv_k, p.q_bf16, kv->head_dim, nt, grid, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+  return PA_OK;
+}
+
+int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, void* stream) {
+  if (p.B == 0 || p.maxq == 0) return PA_OK;
+  if (p.B > 65535) return fail(PA_ERR_UNSUPPORTED, "prefill kernel supports at most 65535 sequences per call");
+  cudaError_t e = pa::launch_prefill(p, kv_kind(kv->dtype), kv->head_dim, kv->dtype == PA_DTYPE_BF16,
+                                     static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
+  return PA_OK;
+}
+
+int build_write(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                pa::WriteParams& w) {
+  int rc = check_cache(kv);
+  if (rc) return rc;
+  if (!pg) return fail(PA_ERR_INVALID, "paging descriptor is NULL");
+  if (!nw) return fail(PA_ERR_INVALID, "new K/V descriptor is NULL");
+  if (nw->dtype != PA_DTYPE_F16 && nw->dtype != PA_DTYPE_BF16 && nw->dtype != PA_DTYPE_F32)
+    return fail(PA_ERR_INVALID, "new K/V dtype must be fp16, bf16 or fp32");
+  if (nw->num_tokens < 0) return fail(PA_ERR_INVALID, "num_tokens < 0");
+  const int e = elt_size(nw->dtype);
+  if (nw->num_tokens > 0) {
+    if (!nw->k_new || !nw->v_new || !nw->seq_index || !nw->positions || !pg->block_table)
+      return fail(PA_ERR_INVALID, "write: NULL pointer");
+    if (!al(nw->k_new, 16) || !al(nw->v_new, 16) || !row_al(nw->k_stride_token, e, 16) ||
+        !row_al(nw->k_stride_head, e, 16) || !row_al(nw->v_stride_token, e, 16) || !row_al(nw->v_stride_head, e, 16))
+      return fail(PA_ERR_INVALID, "new K/V rows must be 16-byte aligned (contiguous head_dim)");
+  }
+  w = pa::WriteParams{};
+  w.k_new = nw->k_new;
+  w.v_new = nw->v_new;
+  w.kn_st = nw->k_stride_token;
+  w.kn_sh = nw->k_stride_head;
+  w.vn_st = nw->v_stride_token;
+  w.vn_sh = nw->v_stride_head;
+  w.in_dtype = nw->dtype;
+  w.seq_idx = nw->seq_index;
+  w.pos = nw->positions;
+  w.T = nw->num_tokens;
+  w.bt = pg->block_table;
+  w.bt_ss = pg->bt_stride_seq;
+  w.bt_sc = pg->bt_stride_col;
+  w.bt_cols = pg->bt_cols;
+  w.num_seqs = pg->num_seqs;
+  w.k = kv->k;
+  w.v = kv->v;
+  w.k_sblk = kv->k_stride_block;
+  w.k_sslot = kv->k_stride_slot;
+  w.k_shead = kv->k_stride_head;
+  w.v_sblk = kv->v_stride_block;
+  w.v_sslot = kv->v_stride_slot;
+  w.v_shead = kv->v_stride_head;
+  w.cache_dtype = kv->dtype;
+  w.ks = kv->k_scale;
+  w.vs = kv->v_scale;
+  w.ks_sblk = kv->ks_stride_block;
+  w.ks_sslot = kv->ks_stride_slot;
+  w.ks_shead = kv->ks_stride_head;
+  w.vs_sblk = kv->vs_stride_block;
+  w.vs_sslot = kv->vs_stride_slot;
+  w.vs_shead = kv->vs_stride_head;
+  w.scale_f32 = kv->scale_dtype == PA_DTYPE_F32;
+  w.Hkv = kv->num_kv_heads;
+  w.D = kv->head_dim;
+  w.BS = kv->block_size;
+  w.log2BS = ilog2(kv->block_size);
+  w.NB = kv->num_blocks;
+  w.status = status;
+  return PA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg,
+                              size_t* bytes) {
+  g_err[0] = 0;
+  if (!bytes) return fail(PA_ERR_INVALID, "bytes is NULL");
+  *bytes = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, nullptr, p);
+  if (rc) return rc;
+  if (!use_decode(p) || p.B == 0 || p.maxq == 0) return PA_OK;
+  const int grid = cached_grid(kv_kind(kv->dtype), p.q_bf16, kv->head_dim, decode_nt(p), p.B);
+  if (grid <= 0) return fail(PA_ERR_CUDA, "could not size the decode grid (no CUDA device?)");
+  *bytes = ws_layout(grid * pa::decode_warps_per_cta(), kv->head_dim, p.B).total;
+  return PA_OK;
+}
+
+int paged_attn_forward(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                       size_t workspace_bytes, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  if (use_decode(p)) return run_decode(p, kv, workspace, workspace_bytes, stream);
+  return run_prefill(p, kv, stream);
+}
+
+int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  return run_decode(p, kv, workspace, workspace_bytes, stream);
+}
+
+int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                       void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  return run_prefill(p, kv, stream);
+}
+
+int kv_write_quant(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                   void* stream) {
+  g_err[0] = 0;
+  pa::WriteParams w;
+  int rc = build_write(nw, kv, pg, status, w);
+  if (rc) return rc;
+  if (kv->dtype != PA_DTYPE_I8) return fail(PA_ERR_INVALID, "kv_write_quant needs an int8 pool");
+  cudaError_t e = pa::launch_kv_write(w, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_write_quant launch");
+  return PA_OK;
+}
+
+int kv_write_copy(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                  void* stream) {
+  g_err[0] = 0;
+  pa::WriteParams w;
+  int rc = build_write(nw, kv, pg, status, w);
+  if (rc) return rc;
+  if (kv->dtype == PA_DTYPE_I8) return fail(PA_ERR_INVALID, "kv_write_copy needs an fp16 / bf16 pool");
+  cudaError_t e = pa::launch_kv_write(w, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_write_copy launch");
+  return PA_OK;
+}
+
+const char* paged_attn_error_string(void) { return g_err; }
+
+const char* paged_attn_version(void) { return "0.1.0"; }
+
+}  // extern "C"

@@ -1,0 +1,691 @@
+// Split-K ("flash-decoding") paged attention for short query blocks.
+//
+// Replaces the q_len == 1 use of flash_attention_kernel
+// (kernels/flash_attention.py:19-136), whose grid
+// (batch, heads, cdiv(max_q_len, BLOCK_M)) gives one program per (sequence,
+// head) that walks the block table serially (:58) with >= 31 of 32 MMA rows
+// idle, and reads every KV head once per query head.
+//
+// Design (B200, HBM-bound):
+//  * Work unit = a 16-key TILE of one (sequence, kv head) SEGMENT.  All tiles
+//    of all segments form one flat list (segment-major); a persistent grid of
+//    W warps gives warp w the contiguous range [w*chunk, (w+1)*chunk) with
+//    chunk = ceil(total / W) ("stream-K"): every warp streams the same number
+//    of KV bytes however skewed the context lengths are.
+//  * Each warp is an independent worker with a private cp.async ring of
+//    STAGES tiles (K, V and, for INT8, the scale words), so loads for the next
+//    tiles -- also across segment boundaries -- are in flight while the
+//    current tile is computed.  No CTA barrier in the main loop.
+//  * Grouped-query packing: the G = Hq/Hkv query heads (times q_len rows)
+//    of a KV head form the N=8*NT columns of a transposed product
+//    S^T = K * Q^T (mma.sync m16n8k16, keys in M), so each KV tile is read
+//    once per KV head and feeds all its query heads.
+//  * Online softmax in base 2 with the softmax scale folded into one multiply;
+//    P^T goes through 256 bytes of shared memory (ldmatrix.trans) into the B
+//    operand of O^T = V^T * P^T.
+//  * INT8 KV: the tile stays int8 in shared memory; fragments are converted
+//    with an exact prmt/hsub2 int8->fp16 sequence.  The per-key K scale is
+//    applied to the logits and the per-key V scale to P before the PV
+//    product -- algebraically the reference's dequantise-then-dot
+//    (kernels/flash_attention.py:83-88,113).
+//  * A segment split across warps leaves fp32 partials (m, l, o) in the
+//    workspace; pa_decode_merge_kernel combines them.  Segments inside one
+//    warp's range are written straight to O / L.
+#include "pa_common.cuh"
+
+namespace pa {
+namespace {
+
+constexpr int TILE = 16;
+constexpr int NC_MAX = 16;  // max packed columns (q rows x group heads)
+constexpr int DEC_NW = 4;   // warps per CTA
+
+template <int D, int KVT>
+struct DecCfg {
+  static constexpr bool INT8 = KVT == KV_I8;
+  static constexpr int ELT = INT8 ? 1 : 2;
+  static constexpr int ROWB = D * ELT;
+  static constexpr int CHUNKS = ROWB / 16;
+  static constexpr int TILEB = TILE * ROWB;
+  static constexpr int SCB = INT8 ? 144 : 0;  // 32 scale words + half-select mask (padded)
+  static constexpr int STAGEB = 2 * TILEB + SCB;
+  static constexpr int STAGES_RAW = (32 * 1024) / STAGEB;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
+  static constexpr int ROWS_PER_IT = 32 / CHUNKS;
+  static constexpr int LOAD_ITS = TILE / ROWS_PER_IT;
+};
+
+// Shared-memory chunk swizzles (16-byte units) that make the fragment reads
+// below bank-conflict free.
+template <int D, int KVT>
+__device__ __forceinline__ int swz_k(int row, int c) {
+  if constexpr (KVT != KV_I8) return c ^ (row & 7);
+  else if constexpr (D >= 128) return c ^ ((row & 1) << 2);
+  else return c;
+}
+template <int D, int KVT>
+__device__ __forceinline__ int swz_v(int row, int c) {
+  if constexpr (KVT != KV_I8) return c ^ (row & 7);
+  else if constexpr (D >= 128) return c ^ (((row >> 1) & 3) << 1);
+  else return c ^ ((row >> 1) & 3);
+}
+
+// Query rows of sequence b, never more than the rows Q holds.
+__device__ __forceinline__ int seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
+
+__device__ __forceinline__ int seq_keys(const AttnParams& p, int b) {
+  const int q = seq_qlen(p, b);
+  if (q <= 0) return 0;
+  int nb = p.nblk[b];
+  if (nb > p.bt_cols) nb = p.bt_cols;
+  if (nb < 0) nb = 0;
+  long long nk = p.kvlen[b];
+  const long long cap = static_cast<long long>(nb) << p.log2BS;
+  if (nk > cap) nk = cap;
+  if (nk < 0) nk = 0;
+  if (p.top_left && nk > q) nk = q;
+  return static_cast<int>(nk);
+}
+
+struct Cursor {
+  int b, kvh, tile, nt;
+  int nkeys;
+  const int* bt_row;
+};
+
+__device__ __forceinline__ void cursor_seq(const AttnParams& p, const int* ts, Cursor& c) {
+  c.nt = ts[c.b + 1] - ts[c.b];
+  c.nkeys = seq_keys(p, c.b);
+  c.bt_row = p.bt + static_cast<long long>(c.b) * p.bt_ss;
+}
+
+__device__ __forceinline__ void cursor_locate(const AttnParams& p, const int* ts, int g, Cursor& c) {
+  int lo = 0, hi = p.B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (ts[mid] * p.Hkv <= g) lo = mid;
+    else hi = mid - 1;
+  }
+  c.b = lo;
+  cursor_seq(p, ts, c);
+  const int rem = g - ts[lo] * p.Hkv;
+  c.kvh = rem / c.nt;
+  c.tile = rem - c.kvh * c.nt;
+}
+
+__device__ __forceinline__ void cursor_next(const AttnParams& p, const int* ts, Cursor& c) {
+  if (++c.tile < c.nt) return;
+  c.tile = 0;
+  if (++c.kvh < p.Hkv) return;
+  c.kvh = 0;
+  do {
+    ++c.b;
+  } while (c.b < p.B && ts[c.b + 1] == ts[c.b]);
+  if (c.b < p.B) cursor_seq(p, ts, c);
+}
+
+// Issue the cp.async copies of one tile (K, V, scales) into stage `st`.
+template <int D, int KVT>
+__device__ __forceinline__ void load_tile(const AttnParams& p, const Cursor& c, unsigned char* st, int lane) {
+  using C = DecCfg<D, KVT>;
+  const int key0 = c.tile * TILE;
+  const char* kbase = static_cast<const char*>(p.k);
+  const char* vbase = static_cast<const char*>(p.v);
+  const uint32_t sk = smem_u32(st);
+  const uint32_t sv = sk + C::TILEB;
+  const int ch = lane % C::CHUNKS;
+#pragma unroll
+  for (int it = 0; it < C::LOAD_ITS; ++it) {
+    const int row = it * C::ROWS_PER_IT + lane / C::CHUNKS;
+    const int key = key0 + row;
+    bool ok = key < c.nkeys;
+    int blk = 0, slot = 0;
+    if (ok) {
+      blk = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+      slot = key & (p.BS - 1);
+      if (blk < 0 || blk >= p.NB) {
+        set_status(p.status, ST_BAD_BLOCK_ID);
+        ok = false;
+      }
+    }
+    const char* ksrc = kbase;
+    const char* vsrc = vbase;
+    if (ok) {
+      ksrc = kbase + (blk * p.k_sblk + slot * p.k_sslot + c.kvh * p.k_shead) * C::ELT + ch * 16;
+      vsrc = vbase + (blk * p.v_sblk + slot * p.v_sslot + c.kvh * p.v_shead) * C::ELT + ch * 16;
+    }
+    cp_async_16(sk + row * C::ROWB + swz_k<D, KVT>(row, ch) * 16, ksrc, ok ? 16 : 0);
+    cp_async_16(sv + row * C::ROWB + swz_v<D, KVT>(row, ch) * 16, vsrc, ok ? 16 : 0);
+  }
+  if constexpr (C::INT8) {
+    // lanes 0..15: K scale of rows 0..15, lanes 16..31: V scale.
+    const int row = lane & 15;
+    const int key = key0 + row;
+    bool ok = key < c.nkeys;
+    int blk = 0, slot = 0;
+    if (ok) {
+      blk = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+      slot = key & (p.BS - 1);
+      ok = blk >= 0 && blk < p.NB;
+    }
+    const bool isv = lane >= 16;
+    const char* sbase = static_cast<const char*>(isv ? p.vs : p.ks);
+    unsigned long long addr = reinterpret_cast<unsigned long long>(sbase);
+    if (ok) {
+      const long long off = isv ? (blk * p.vs_sblk + slot * p.vs_sslot + c.kvh * p.vs_shead)
+                                : (blk * p.ks_sblk + slot * p.ks_sslot + c.kvh * p.ks_shead);
+      addr += static_cast<unsigned long long>(off) * (p.scale_f32 ? 4 : 2);
+    }
+    const unsigned hi = (!p.scale_f32 && ((addr >> 1) & 1)) ? 1u : 0u;
+    const unsigned mask = __ballot_sync(0xffffffffu, hi);
+    const uint32_t ss = sv + C::TILEB;
+    cp_async_4(ss + lane * 4, reinterpret_cast<const void*>(addr & ~3ull), ok ? 4 : 0);
+    if (lane == 0) *reinterpret_cast<unsigned*>(st + 2 * C::TILEB + 128) = mask;
+  }
+}
+
+__device__ __forceinline__ float scale_from_word(uint32_t w, bool hi, int is_f32) {
+  if (is_f32) return __uint_as_float(w);
+  const unsigned short h = hi ? static_cast<unsigned short>(w >> 16) : static_cast<unsigned short>(w & 0xffffu);
+  return __half2float(__ushort_as_half(h));
+}
+
+template <int D, int KVT, int QT, int NT, int STAGES>
+__global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnParams p) {
+  using C = DecCfg<D, KVT>;
+  constexpr bool INT8 = C::INT8;
+  constexpr bool MMA_BF16 = (KVT == KV_BF16);
+  constexpr bool QIS_BF16 = (QT == Q_BF16);
+  constexpr int KS = D / 16;  // k-steps over head_dim / m-tiles of O^T
+  constexpr int NC = 8 * NT;
+  constexpr int PB = TILE * NC * 2;
+  constexpr int WARPB = STAGES * C::STAGEB + PB;
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  int* s_ts = reinterpret_cast<int*>(smem);
+  const int ts_bytes = ((p.B + 1) * 4 + 127) & ~127;
+  unsigned char* wsm = smem + ts_bytes + warp * WARPB;
+  unsigned char* pbuf = wsm + STAGES * C::STAGEB;
+
+  // ---- prologue: tiles per sequence and their exclusive scan -------------
+  for (int i = tid; i < p.B; i += DEC_NW * 32) {
+    const int nk = seq_keys(p, i);
+    if (p.nblk[i] > p.bt_cols) set_status(p.status, ST_BAD_NUM_BLOCKS);
+    s_ts[i] = (nk + TILE - 1) / TILE;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < p.B; base += 32) {
+      const int i = base + lane;
+      const int v = i < p.B ? s_ts[i] : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (i < p.B) s_ts[i] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) s_ts[p.B] = carry;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int i = tid; i <= p.B; i += DEC_NW * 32) p.tstart[i] = s_ts[i];
+  }
+
+  const int total = s_ts[p.B] * p.Hkv;
+  const int W = p.num_warps_total;
+  const int chunk = (total + W - 1) / W;
+  const int gw = blockIdx.x * DEC_NW + warp;
+  const int g0 = gw * chunk;
+  const int g1 = min(g0 + chunk, total);
+  if (total == 0 || g0 >= g1) return;
+
+  const int r = lane >> 2;  // fragment row group
+  const int q4 = lane & 3;  // thread in group
+
+  Cursor ld, cp;
+  cursor_locate(p, s_ts, g0, ld);
+  cp = ld;
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (g0 + s < g1) {
+      load_tile<D, KVT>(p, ld, wsm + s * C::STAGEB, lane);
+      cursor_next(p, s_ts, ld);
+    }
+    cp_async_commit();
+  }
+
+  uint32_t qf[NT][KS][2];
+  float acc[KS][NT][4];
+  float m_run[NT][2], l_run[NT][2];
+  int lim[NT][2];
+  int piece_start_tile = 0;
+  bool piece_first = true;  // first piece of this warp's range
+
+  for (int g = g0; g < g1; ++g) {
+    const int i = g - g0;
+    // ---- prefetch tile i + STAGES - 1 into the slot freed last iteration --
+    __syncwarp();
+    if (g + STAGES - 1 < g1) {
+      load_tile<D, KVT>(p, ld, wsm + ((i + STAGES - 1) % STAGES) * C::STAGEB, lane);
+      cursor_next(p, s_ts, ld);
+    }
+    cp_async_commit();
+
+    const bool pstart = (g == g0) || (cp.tile == 0);
+    const bool pend = (g == g1 - 1) || (cp.tile == cp.nt - 1);
+    const int qlen_b = seq_qlen(p, cp.b);
+    if (pstart) {
+      piece_start_tile = cp.tile;
+      // ---- Q^T fragments of the packed (q row, group head) columns -------
+      const int off = p.top_left ? 0 : (p.kvlen[cp.b] - qlen_b);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int col = nt * 8 + r;
+        const int qi = col / p.G;
+        const int hq = col - qi * p.G;
+        const bool valid = qi < qlen_b;
+        const unsigned short* qrow = static_cast<const unsigned short*>(p.q) + cp.b * p.q_sb +
+                                     (cp.kvh * p.G + hq) * p.q_sh + static_cast<long long>(qi) * p.q_sm;
+        if constexpr (!INT8) {
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk) {
+            uint32_t w0 = 0, w1 = 0;
+            if (valid) {
+              w0 = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 2 * q4);
+              w1 = *reinterpret_cast<const uint32_t*>(qrow + 16 * kk + 8 + 2 * q4);
+            }
+            qf[nt][kk][0] = cvt_pair<QIS_BF16, MMA_BF16>(w0);
+            qf[nt][kk][1] = cvt_pair<QIS_BF16, MMA_BF16>(w1);
+          }
+        } else {
+#pragma unroll
+          for (int gg = 0; gg < D / 64; ++gg) {
+            uint4 a = make_uint4(0, 0, 0, 0), bq = make_uint4(0, 0, 0, 0);
+            if (valid) {
+              const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * gg + 16 * q4);
+              a = src[0];
+              bq = src[1];
+            }
+            const uint32_t w[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              qf[nt][4 * gg + j][0] = cvt_pair<QIS_BF16, false>(w[2 * j]);
+              qf[nt][4 * gg + j][1] = cvt_pair<QIS_BF16, false>(w[2 * j + 1]);
+            }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c2 = nt * 8 + 2 * q4 + e;
+          const int qi2 = c2 / p.G;
+          int L = cp.nkeys;
+          if (qi2 < qlen_b) {
+            const int vis = off + qi2 + 1;
+            L = min(L, vis);
+          }
+          lim[nt][e] = L;
+          m_run[nt][e] = -INFINITY;
+          l_run[nt][e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[mt][nt][c] = 0.f;
+    }
+
+    // ---- wait for this tile ----------------------------------------------
+    cp_async_wait<STAGES - 1>();
+    __syncwarp();
+    unsigned char* st = wsm + (i % STAGES) * C::STAGEB;
+    const uint32_t sk = smem_u32(st);
+    const uint32_t sv = sk + C::TILEB;
+
+    // ---- S^T = K * Q^T -----------------------------------------------------
+    float s[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[nt][c] = 0.f;
+    if constexpr (!INT8) {
+      const int j = lane >> 3;
+      const int row = (lane & 7) + 8 * (j & 1);
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        uint32_t a[4];
+        const int chn = 2 * kk + (j >> 1);
+        ldsm_x4(sk + row * C::ROWB + swz_k<D, KVT>(row, chn) * 16, a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(s[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+      }
+    } else {
+#pragma unroll
+      for (int gg = 0; gg < D / 64; ++gg) {
+        const int chn = 4 * gg + q4;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(st + r * C::ROWB + swz_k<D, KVT>(r, chn) * 16);
+        const uint4 w1 =
+            *reinterpret_cast<const uint4*>(st + (r + 8) * C::ROWB + swz_k<D, KVT>(r + 8, chn) * 16);
+        const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w};
+        const uint32_t x1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          uint32_t a[4];
+          i8x4_to_f16x4(x0[jj], a[0], a[2]);
+          i8x4_to_f16x4(x1[jj], a[1], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma16816<false>(s[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+        }
+      }
+    }
+
+    // ---- scales (INT8) --------------------------------------------------
+    float ksc0 = 1.f, ksc1 = 1.f, vsc0 = 1.f, vsc1 = 1.f;
+    if constexpr (INT8) {
+      const uint32_t* sw = reinterpret_cast<const uint32_t*>(st + 2 * C::TILEB);
+      const unsigned hm = *reinterpret_cast<const unsigned*>(st + 2 * C::TILEB + 128);
+      ksc0 = scale_from_word(sw[r], (hm >> r) & 1, p.scale_f32);
+      ksc1 = scale_from_word(sw[r + 8], (hm >> (r + 8)) & 1, p.scale_f32);
+      vsc0 = scale_from_word(sw[16 + r], (hm >> (16 + r)) & 1, p.scale_f32);
+      vsc1 = scale_from_word(sw[24 + r], (hm >> (24 + r)) & 1, p.scale_f32);
+    }
+
+    // ---- online softmax (base 2) ------------------------------------------
+    const int key_a = cp.tile * TILE + r;
+    const int key_b = key_a + 8;
+    uint32_t* pw = reinterpret_cast<uint32_t*>(pbuf);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float pv[4];
+      float alpha[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float x0 = s[nt][e] * ksc0 * p.scale_log2;
+        float x1 = s[nt][2 + e] * ksc1 * p.scale_log2;
+        if (key_a >= lim[nt][e]) x0 = -INFINITY;
+        if (key_b >= lim[nt][e]) x1 = -INFINITY;
+        const float tmax = warp_max_xor(fmaxf(x0, x1), 4);
+        const float m_new = fmaxf(m_run[nt][e], tmax);
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        alpha[e] = ex2(m_run[nt][e] - m_use);
+        const float p0 = ex2(x0 - m_use);
+        const float p1 = ex2(x1 - m_use);
+        l_run[nt][e] = l_run[nt][e] * alpha[e] + p0 + p1;
+        m_run[nt][e] = m_new;
+        pv[e] = p0;
+        pv[2 + e] = p1;
+      }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        acc[mt][nt][0] *= alpha[0];
+        acc[mt][nt][1] *= alpha[1];
+        acc[mt][nt][2] *= alpha[0];
+        acc[mt][nt][3] *= alpha[1];
+      }
+      // P^T tile [key][col] (fp16 or bf16, V scale folded in for INT8)
+      pw[(r * NC + nt * 8 + 2 * q4) >> 1] = pack2<MMA_BF16>(pv[0] * vsc0, pv[1] * vsc0);
+      pw[((r + 8) * NC + nt * 8 + 2 * q4) >> 1] = pack2<MMA_BF16>(pv[2] * vsc1, pv[3] * vsc1);
+    }
+    __syncwarp();
+    uint32_t bp[NT][2];
+    {
+      const uint32_t pb = smem_u32(pbuf);
+      if constexpr (NT == 1) {
+        ldsm_x2_t(pb + (lane & 15) * NC * 2, bp[0][0], bp[0][1]);
+      } else {
+        const int row = lane & 15;
+        const int colb = (lane >> 4) * 8;
+        ldsm_x4_t(pb + (row * NC + colb) * 2, bp[0][0], bp[0][1], bp[1][0], bp[1][1]);
+      }
+    }
+
+    // ---- O^T += V^T * P^T ---------------------------------------------------
+    if constexpr (!INT8) {
+      const int j = lane >> 3;
+      const int row = (lane & 7) + 8 * (j >> 1);
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt) {
+        uint32_t a[4];
+        const int chn = 2 * mt + (j & 1);
+        ldsm_x4_t(sv + row * C::ROWB + swz_v<D, KVT>(row, chn) * 16, a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(acc[mt][nt], a, bp[nt][0], bp[nt][1]);
+      }
+    } else {
+      const unsigned char* vt = st + C::TILEB;
+      constexpr int WORDS = D / 32;  // 32-bit words of this thread's d range per key
+      uint32_t R[4][WORDS];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int row = 2 * q4 + (c & 1) + 8 * (c >> 1);
+        if constexpr (D >= 128) {
+          const uint4 w = *reinterpret_cast<const uint4*>(vt + row * C::ROWB + swz_v<D, KVT>(row, r) * 16);
+          R[c][0] = w.x;
+          R[c][1] = w.y;
+          R[c][2] = w.z;
+          R[c][3] = w.w;
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(vt + row * C::ROWB + swz_v<D, KVT>(row, r >> 1) * 16 +
+                                                          (r & 1) * 8);
+          R[c][0] = w.x;
+          R[c][1] = w.y;
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < WORDS; ++w) {
+        const uint32_t x01 = prmt(R[0][w], R[1][w], 0x5140u);
+        const uint32_t y01 = prmt(R[0][w], R[1][w], 0x7362u);
+        const uint32_t x23 = prmt(R[2][w], R[3][w], 0x5140u);
+        const uint32_t y23 = prmt(R[2][w], R[3][w], 0x7362u);
+        uint32_t a[4], b2[4];
+        i8x4_to_f16x4(x01, a[0], a[1]);
+        i8x4_to_f16x4(x23, a[2], a[3]);
+        i8x4_to_f16x4(y01, b2[0], b2[1]);
+        i8x4_to_f16x4(y23, b2[2], b2[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma16816<false>(acc[2 * w][nt], a, bp[nt][0], bp[nt][1]);
+          mma16816<false>(acc[2 * w + 1][nt], b2, bp[nt][0], bp[nt][1]);
+        }
+      }
+    }
+
+    // ---- end of a piece: final output or split-K partial ------------------
+    if (pend) {
+      const bool complete = (piece_start_tile == 0) && (cp.tile == cp.nt - 1);
+      const int slot = piece_first ? 2 * gw : 2 * gw + 1;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float lt = warp_sum_xor(l_run[nt][e], 4);
+          const int col = nt * 8 + 2 * q4 + e;
+          const int qi = col / p.G;
+          const int hq = col - qi * p.G;
+          const bool valid = (qi < qlen_b) && (col < NC);
+          if (complete) {
+            const float inv = lt > 0.f ? 1.f / lt : 0.f;
+            if (valid) {
+              __half* orow = static_cast<__half*>(p.o) + cp.b * p.o_sb + (cp.kvh * p.G + hq) * p.o_sh +
+                             static_cast<long long>(qi) * p.o_sm;
+#pragma unroll
+              for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                  const int d = INT8 ? (D / 8) * r + 2 * mt + hf : 16 * mt + r + 8 * hf;
+                  orow[d] = __float2half_rn(acc[mt][nt][e + 2 * hf] * inv);
+                }
+              if (r == 0 && p.lse) {
+                const float L = lt > 0.f ? (m_run[nt][e] + lg2(lt)) * 0.6931471805599453f : -INFINITY;
+                static_cast<__half*>(p.lse)[cp.b * p.l_sb + (cp.kvh * p.G + hq) * p.l_sh +
+                                            static_cast<long long>(qi) * p.l_sm] = __float2half_rn(L);
+              }
+            }
+          } else {
+            float* po = p.part_o + (static_cast<long long>(slot) * NC_MAX + col) * D;
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const int d = INT8 ? (D / 8) * r + 2 * mt + hf : 16 * mt + r + 8 * hf;
+                po[d] = acc[mt][nt][e + 2 * hf];
+              }
+            if (r == 0) {
+              float* pm = p.part_ml + (static_cast<long long>(slot) * NC_MAX + col) * 2;
+              pm[0] = m_run[nt][e];
+              pm[1] = lt;
+            }
+          }
+        }
+      }
+      piece_first = false;
+    }
+    cursor_next(p, s_ts, cp);
+  }
+  cp_async_wait<0>();
+}
+
+// Combine the split-K partials of every segment that straddles warp ranges.
+// grid (Hkv, B), 128 threads.
+template <int D>
+__global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p) {
+  const int kvh = blockIdx.x;
+  const int b = blockIdx.y;
+  const int qlen = seq_qlen(p, b);
+  if (qlen <= 0) return;
+  const int ncols = min(qlen * p.G, NC_MAX);
+  const int nt_b = p.tstart[b + 1] - p.tstart[b];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (nt_b == 0) {
+    // no visible keys: O = 0, L = -inf
+    for (int col = warp; col < ncols; col += 4) {
+      const int qi = col / p.G, hq = col - (col / p.G) * p.G;
+      __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + (kvh * p.G + hq) * p.o_sh +
+                     static_cast<long long>(qi) * p.o_sm;
+      for (int d = lane; d < D; d += 32) orow[d] = __float2half_rn(0.f);
+      if (lane == 0 && p.lse)
+        static_cast<__half*>(p.lse)[b * p.l_sb + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
+            __float2half_rn(-INFINITY);
+    }
+    return;
+  }
+  const int total = p.tstart[p.B] * p.Hkv;
+  const int W = p.num_warps_total;
+  const int chunk = (total + W - 1) / W;
+  const int S0 = p.tstart[b] * p.Hkv + kvh * nt_b;
+  const int S1 = S0 + nt_b;
+  const int w0 = S0 / chunk;
+  const int w1 = (S1 - 1) / chunk;
+  if (w0 == w1) return;  // written directly by the split kernel
+  for (int col = warp; col < ncols; col += 4) {
+    const int qi = col / p.G, hq = col - (col / p.G) * p.G;
+    float M = -INFINITY;
+    for (int w = w0; w <= w1; ++w) {
+      const int slot = (w == w0 && w0 * chunk < S0) ? 2 * w + 1 : 2 * w;
+      M = fmaxf(M, p.part_ml[(static_cast<long long>(slot) * NC_MAX + col) * 2]);
+    }
+    const float Mu = (M == -INFINITY) ? 0.f : M;
+    float l = 0.f;
+    float o[D / 32];
+#pragma unroll
+    for (int k = 0; k < D / 32; ++k) o[k] = 0.f;
+    for (int w = w0; w <= w1; ++w) {
+      const int slot = (w == w0 && w0 * chunk < S0) ? 2 * w + 1 : 2 * w;
+      const float* pm = p.part_ml + (static_cast<long long>(slot) * NC_MAX + col) * 2;
+      const float f = ex2(pm[0] - Mu);
+      l += pm[1] * f;
+      const float* po = p.part_o + (static_cast<long long>(slot) * NC_MAX + col) * D;
+#pragma unroll
+      for (int k = 0; k < D / 32; ++k) o[k] += po[lane + 32 * k] * f;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + (kvh * p.G + hq) * p.o_sh +
+                   static_cast<long long>(qi) * p.o_sm;
+#pragma unroll
+    for (int k = 0; k < D / 32; ++k) orow[lane + 32 * k] = __float2half_rn(o[k] * inv);
+    if (lane == 0 && p.lse) {
+      const float L = l > 0.f ? (M + lg2(l)) * 0.6931471805599453f : -INFINITY;
+      static_cast<__half*>(p.lse)[b * p.l_sb + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
+          __float2half_rn(L);
+    }
+  }
+}
+
+template <int D, int KVT, int QT, int NT>
+struct DecodeInst {
+  using C = DecCfg<D, KVT>;
+  static constexpr int STAGES = C::STAGES;
+  static constexpr int WARPB = STAGES * C::STAGEB + TILE * 8 * NT * 2;
+  static size_t smem_bytes(int B) { return static_cast<size_t>(((B + 1) * 4 + 127) & ~127) + DEC_NW * WARPB; }
+  static int grid(int B) {
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto kern = pa_decode_kernel<D, KVT, QT, NT, STAGES>;
+    const size_t sm = smem_bytes(B);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DEC_NW * 32, sm);
+    if (per_sm < 1) per_sm = 1;
+    return sms * per_sm;
+  }
+  static cudaError_t launch(const AttnParams& p, cudaStream_t stream, int grid_ctas) {
+    auto kern = pa_decode_kernel<D, KVT, QT, NT, STAGES>;
+    const size_t sm = smem_bytes(p.B);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+    kern<<<grid_ctas, DEC_NW * 32, sm, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    pa_decode_merge_kernel<D><<<dim3(p.Hkv, p.B), 128, 0, stream>>>(p);
+    return cudaGetLastError();
+  }
+};
+
+template <int D, int KVT, int QT>
+int grid_nt(int nt, int B) {
+  return nt == 1 ? DecodeInst<D, KVT, QT, 1>::grid(B) : DecodeInst<D, KVT, QT, 2>::grid(B);
+}
+template <int D, int KVT, int QT>
+cudaError_t launch_nt(const AttnParams& p, int nt, int grid, cudaStream_t s) {
+  return nt == 1 ? DecodeInst<D, KVT, QT, 1>::launch(p, s, grid) : DecodeInst<D, KVT, QT, 2>::launch(p, s, grid);
+}
+template <int D>
+int grid_kv(int kv, int qbf, int nt, int B) {
+  if (kv == KV_F16) return qbf ? grid_nt<D, KV_F16, Q_BF16>(nt, B) : grid_nt<D, KV_F16, Q_F16>(nt, B);
+  if (kv == KV_BF16) return qbf ? grid_nt<D, KV_BF16, Q_BF16>(nt, B) : grid_nt<D, KV_BF16, Q_F16>(nt, B);
+  return qbf ? grid_nt<D, KV_I8, Q_BF16>(nt, B) : grid_nt<D, KV_I8, Q_F16>(nt, B);
+}
+template <int D>
+cudaError_t launch_kv(const AttnParams& p, int kv, int qbf, int nt, int grid, cudaStream_t s) {
+  if (kv == KV_F16) return qbf ? launch_nt<D, KV_F16, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_F16, Q_F16>(p, nt, grid, s);
+  if (kv == KV_BF16) return qbf ? launch_nt<D, KV_BF16, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_BF16, Q_F16>(p, nt, grid, s);
+  return qbf ? launch_nt<D, KV_I8, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_I8, Q_F16>(p, nt, grid, s);
+}
+
+}  // namespace
+
+int decode_warps_per_cta() { return DEC_NW; }
+
+int decode_grid_size(int kv_kind, int q_bf16, int D, int nt, int B) {
+  if (D == 64) return grid_kv<64>(kv_kind, q_bf16, nt, B);
+  if (D == 128) return grid_kv<128>(kv_kind, q_bf16, nt, B);
+  return 0;
+}
+
+cudaError_t launch_decode(const AttnParams& p, int kv_kind, int q_bf16, int D, int nt, int grid, cudaStream_t stream) {
+  if (D == 64) return launch_kv<64>(p, kv_kind, q_bf16, nt, grid, stream);
+  if (D == 128) return launch_kv<128>(p, kv_kind, q_bf16, nt, grid, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace pa

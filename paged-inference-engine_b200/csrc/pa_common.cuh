@@ -1,0 +1,157 @@
+// Shared device helpers for the sm_100a paged-attention kernels.
+//
+// Everything here is a thin wrapper over a documented PTX instruction
+// (mma.sync, ldmatrix, cp.async, ex2.approx, prmt) or plain integer/float
+// arithmetic.  No CUDA math-library routine is restated.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "pa_types.h"
+
+namespace pa {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// cp.async (Ampere-style asynchronous global->shared copies).
+// src_bytes == 0 zero-fills the destination without touching global memory,
+// which is how masked / out-of-range rows become zeros in shared memory.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---------------------------------------------------------------------------
+// ldmatrix / mma.sync (m16n8k16, fp32 accumulate).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Scalar helpers.
+// ---------------------------------------------------------------------------
+// Hardware base-2 exponential (MUFU.EX2); ex2(-inf) == +0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Four signed int8 values (bytes 0..3 of `w`) -> two packed fp16 pairs
+// {b0,b1} and {b2,b3}.  Exact for every int8 input: the byte is biased to
+// unsigned (xor 0x80), placed in the mantissa of 1024.0h (0x64xx) and the
+// bias 1024+128 is subtracted.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  uint32_t a = prmt(u, 0x64646464u, 0x5140u);
+  uint32_t b = prmt(u, 0x64646464u, 0x7362u);
+  const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+  __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
+  __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
+  lo = *reinterpret_cast<uint32_t*>(&ha);
+  hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) return pack_bf16(a, b);
+  else return pack_f16(a, b);
+}
+
+// Convert a packed pair of 16-bit values of element type SRC_BF16 into the
+// MMA element type DST_BF16 (identity when equal).
+template <bool SRC_BF16, bool DST_BF16>
+__device__ __forceinline__ uint32_t cvt_pair(uint32_t v) {
+  if constexpr (SRC_BF16 == DST_BF16) {
+    return v;
+  } else if constexpr (SRC_BF16) {
+    float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+    return pack_f16(f.x, f.y);
+  } else {
+    float2 f = __half22float2(*reinterpret_cast<__half2*>(&v));
+    return pack_bf16(f.x, f.y);
+  }
+}
+
+__device__ __forceinline__ float warp_max_xor(float v, int first_mask) {
+  for (int m = first_mask; m < 32; m <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_xor(float v, int first_mask) {
+  for (int m = first_mask; m < 32; m <<= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+__device__ __forceinline__ void set_status(int* status, int bit) {
+  if (status) atomicOr(status, bit);
+}
+
+__device__ __forceinline__ float load_scale(const void* base, long long off, int is_f32) {
+  return is_f32 ? static_cast<const float*>(base)[off]
+                : __half2float(static_cast<const __half*>(base)[off]);
+}
+
+}  // namespace pa

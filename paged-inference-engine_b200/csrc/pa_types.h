@@ -1,0 +1,100 @@
+// Internal parameter blocks shared by the C-ABI layer (capi.cu) and the
+// kernels.  Plain C structs: pointers, element strides and sizes only.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "paged_attn_b200.h"
+
+namespace pa {
+
+// Element types of the KV pool / Q operand (kernel template tags).
+enum : int { KV_F16 = 0, KV_BF16 = 1, KV_I8 = 2 };
+enum : int { Q_F16 = 0, Q_BF16 = 1 };
+
+// Device-side status bits (OR-ed into the optional status word).
+enum : int {
+  ST_BAD_BLOCK_ID = 1,     // block table entry outside [0, num_pool_blocks)
+  ST_BAD_POSITION = 2,     // write position beyond the block table row
+  ST_BAD_NUM_BLOCKS = 4,   // num_blocks_per_seq larger than the block table width
+  ST_BAD_SEQ_INDEX = 8,    // token -> sequence index outside [0, num_seqs)
+};
+
+struct AttnParams {
+  // Q [B, Hq, maxq, D] (head_dim contiguous)
+  const void* q;
+  long long q_sb, q_sh, q_sm;
+  int q_bf16;
+  // KV pool, logical [block, slot, head, d]
+  const void* k;
+  const void* v;
+  long long k_sblk, k_sslot, k_shead;
+  long long v_sblk, v_sslot, v_shead;
+  // Dequantisation scales (int8 pools); slot stride 0 => one scale per (block, head)
+  const void* ks;
+  const void* vs;
+  long long ks_sblk, ks_sslot, ks_shead;
+  long long vs_sblk, vs_sslot, vs_shead;
+  int scale_f32;
+  // Paging metadata
+  const int* bt;
+  long long bt_ss, bt_sc;
+  int bt_cols;
+  const int* nblk;
+  const int* qlen;
+  const int* kvlen;
+  // Outputs: O [B, Hq, maxq, D] fp16, L [B, Hq, maxq] fp16
+  void* o;
+  long long o_sb, o_sh, o_sm;
+  void* lse;
+  long long l_sb, l_sh, l_sm;
+  // Split-K workspace
+  float* part_o;
+  float* part_ml;
+  int* tstart;
+  int num_warps_total;  // decode: warps of the persistent grid
+  // Shapes
+  int B, Hq, Hkv, G, BS, log2BS, NB, maxq;
+  float scale_log2;  // softmax scale * log2(e)
+  float sm_scale;
+  int top_left;
+  int* status;
+};
+
+struct WriteParams {
+  const void* k_new;
+  const void* v_new;
+  long long kn_st, kn_sh, vn_st, vn_sh;  // [T, Hkv, D] strides (d contiguous)
+  int in_dtype;                          // PA_DTYPE_*
+  const int* seq_idx;                    // [T] row of the block table
+  const int* pos;                        // [T] absolute position in the sequence
+  int T;
+  const int* bt;
+  long long bt_ss, bt_sc;
+  int bt_cols, num_seqs;
+  void* k;
+  void* v;
+  long long k_sblk, k_sslot, k_shead;
+  long long v_sblk, v_sslot, v_shead;
+  int cache_dtype;  // PA_DTYPE_*
+  void* ks;
+  void* vs;
+  long long ks_sblk, ks_sslot, ks_shead;
+  long long vs_sblk, vs_sslot, vs_shead;
+  int scale_f32;
+  int Hkv, D, BS, log2BS, NB;
+  int* status;
+};
+
+// Launchers implemented in the kernel translation units.
+cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream);
+// Decode: persistent grid size (CTAs) for a configuration on the current
+// device, warps per CTA, and the launch of the split kernel + merge kernel.
+int decode_grid_size(int kv_kind, int q_bf16, int D, int nt, int B);
+int decode_warps_per_cta();
+cudaError_t launch_decode(const AttnParams& p, int kv_kind, int q_bf16, int D, int nt, int grid,
+                          cudaStream_t stream);
+cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);
+
+}  // namespace pa
