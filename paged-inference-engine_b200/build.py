@@ -43,6 +43,8 @@ def _compile(nvcc: str, src: str, obj: str, ptxas_info: bool) -> tuple[str, str]
            "-I", CSRC, "-I", INCLUDE, "-c", src, "-o", obj]
     if ptxas_info:
         cmd.insert(1, "-Xptxas=-v")
+    extra = os.environ.get("PIE_B200_NVCC_FLAGS", "").split()
+    cmd[1:1] = extra
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
@@ -60,7 +62,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     for s in srcs:
         o = os.path.join(OBJ_DIR, os.path.basename(s)[:-3] + ".o")
         objs.append(o)
-        stale = force or ptxas_info or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s),
+        stale = force or ptxas_info or bool(os.environ.get("PIE_B200_NVCC_FLAGS")) or not os.path.exists(o) or os.path.getmtime(o) < max(os.path.getmtime(s),
                                                                                            newest_header)
         if stale:
             jobs.append((s, o))

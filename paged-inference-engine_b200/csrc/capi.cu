@@ -3,10 +3,13 @@
 // workspace layout.  Nothing here allocates device memory.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
+
+#include <cudaTypedefs.h>
 
 #include "pa_types.h"
 
@@ -173,22 +176,71 @@ bool use_decode(const pa::AttnParams& p) { return p.maxq * p.G <= kNcMax && p.B 
 int decode_nt(const pa::AttnParams& p) { return p.maxq * p.G <= 8 ? 1 : 2; }
 int kv_kind(int dtype) { return dtype == PA_DTYPE_F16 ? pa::KV_F16 : dtype == PA_DTYPE_BF16 ? pa::KV_BF16 : pa::KV_I8; }
 
-// Persistent decode grid, cached per (device, variant, num_seqs).
-int cached_grid(int kv, int qbf, int D, int nt, int B) {
+// Persistent decode launch plan, cached per (device, variant, num_seqs).
+int cached_plan(int kv, int qbf, int D, int nt, int B, int tma, pa::DecodeLaunch* out) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int, int, int>, int> cache;
+  static std::map<std::tuple<int, int, int, int, int, int, int>, pa::DecodeLaunch> cache;
   int dev = 0;
-  cudaGetDevice(&dev);
-  const auto key = std::make_tuple(dev, kv, qbf, D, nt, B);
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  const auto key = std::make_tuple(dev, kv, qbf, D, nt, B, tma);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
-    if (it != cache.end()) return it->second;
+    if (it != cache.end()) {
+      *out = it->second;
+      return 0;
+    }
   }
-  const int g = pa::decode_grid_size(kv, qbf, D, nt, B);
+  if (pa::decode_plan(kv, qbf, D, nt, B, tma, out) != 0) return -1;
   std::lock_guard<std::mutex> lk(mu);
-  cache[key] = g;
-  return g;
+  cache[key] = *out;
+  return 0;
+}
+
+// cuTensorMapEncodeTiled, fetched through the runtime (no link-time libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D TMA map over a pool read as [block, slot, head, d]: box = 128 bytes of
+// head_dim (64 for 64-byte rows) x 1 head x min(16, block_size) slots x 1 block,
+// with the matching shared-memory swizzle.
+bool make_pool_map(CUtensorMap* m, void* base, int dtype, int D, int H, int BS, int NB, long long s_head,
+                   long long s_slot, long long s_blk) {
+  auto enc = encode_fn();
+  if (!enc || NB < 1 || BS < 8 || s_head <= 0 || s_slot <= 0 || s_blk <= 0) return false;
+  const int elt = dtype == PA_DTYPE_I8 ? 1 : 2;
+  const int rowb = D * elt;
+  if (rowb != 64 && rowb % 128 != 0) return false;
+  const cuuint32_t boxd = static_cast<cuuint32_t>((rowb >= 128 ? 128 : rowb) / elt);
+  const CUtensorMapSwizzle swz = rowb >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(BS),
+                              static_cast<cuuint64_t>(NB)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head * elt), static_cast<cuuint64_t>(s_slot * elt),
+                                 static_cast<cuuint64_t>(s_blk * elt)};
+  const cuuint32_t box[4] = {boxd, 1, static_cast<cuuint32_t>(BS < 16 ? BS : 16), 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, base, dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_kv_maps(const pa_kv_cache_t* kv, pa::KvMaps* maps) {
+  if (std::getenv("PIE_B200_NO_TMA")) return false;
+  return make_pool_map(&maps->k, kv->k, kv->dtype, kv->head_dim, kv->num_kv_heads, kv->block_size, kv->num_blocks,
+                       kv->k_stride_head, kv->k_stride_slot, kv->k_stride_block) &&
+         make_pool_map(&maps->v, kv->v, kv->dtype, kv->head_dim, kv->num_kv_heads, kv->block_size, kv->num_blocks,
+                       kv->v_stride_head, kv->v_stride_slot, kv->v_stride_block);
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
@@ -213,9 +265,12 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
   if (p.B == 0 || p.maxq == 0) return PA_OK;
   const int nt = decode_nt(p);
   const int kv_k = kv_kind(kv->dtype);
-  const int grid = cached_grid(kv_k, p.q_bf16, kv->head_dim, nt, p.B);
-  if (grid <= 0) return fail(PA_ERR_CUDA, "could not size the decode grid (no CUDA device?)");
-  const int warps = grid * pa::decode_warps_per_cta();
+  pa::KvMaps maps;
+  const bool tma = make_kv_maps(kv, &maps);
+  pa::DecodeLaunch plan;
+  if (cached_plan(kv_k, p.q_bf16, kv->head_dim, nt, p.B, tma, &plan) != 0)
+    return fail(PA_ERR_CUDA, "could not plan the decode launch (no CUDA device?)");
+  const int warps = plan.ctas * plan.warps_per_cta;
   const WsLayout L = ws_layout(warps, kv->head_dim, p.B);
   if (!ws || ws_bytes < L.total)
     return fail(PA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", L.total, ws_bytes);
@@ -225,7 +280,8 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
   p.part_ml = reinterpret_cast<float*>(base + L.part_ml);
   p.tstart = reinterpret_cast<int*>(base + L.tstart);
   p.num_warps_total = warps;
-  cudaError_t e = pa::launch_decode(p, kv_k, p.q_bf16, kv->head_dim, nt, grid, static_cast<cudaStream_t>(stream));
+  cudaError_t e = pa::launch_decode(p, tma ? &maps : nullptr, kv_k, p.q_bf16, kv->head_dim, nt, plan,
+                                    static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return PA_OK;
 }
@@ -312,9 +368,12 @@ int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   int rc = build_attn(io, kv, pg, nullptr, p);
   if (rc) return rc;
   if (!use_decode(p) || p.B == 0 || p.maxq == 0) return PA_OK;
-  const int grid = cached_grid(kv_kind(kv->dtype), p.q_bf16, kv->head_dim, decode_nt(p), p.B);
-  if (grid <= 0) return fail(PA_ERR_CUDA, "could not size the decode grid (no CUDA device?)");
-  *bytes = ws_layout(grid * pa::decode_warps_per_cta(), kv->head_dim, p.B).total;
+  pa::KvMaps maps;
+  const bool tma = make_kv_maps(kv, &maps);
+  pa::DecodeLaunch plan;
+  if (cached_plan(kv_kind(kv->dtype), p.q_bf16, kv->head_dim, decode_nt(p), p.B, tma, &plan) != 0)
+    return fail(PA_ERR_CUDA, "could not plan the decode launch (no CUDA device?)");
+  *bytes = ws_layout(plan.ctas * plan.warps_per_cta, kv->head_dim, p.B).total;
   return PA_OK;
 }
 

@@ -12,10 +12,13 @@
 //    W warps gives warp w the contiguous range [w*chunk, (w+1)*chunk) with
 //    chunk = ceil(total / W) ("stream-K"): every warp streams the same number
 //    of KV bytes however skewed the context lengths are.
-//  * Each warp is an independent worker with a private cp.async ring of
-//    STAGES tiles (K, V and, for INT8, the scale words), so loads for the next
-//    tiles -- also across segment boundaries -- are in flight while the
-//    current tile is computed.  No CTA barrier in the main loop.
+//  * Each warp is an independent worker with a private ring of STAGES tiles.
+//    Lane 0 fetches a tile's K and V with TMA boxes (4-D tensor maps over the
+//    pool [block, slot, head, d], 128-byte swizzle, mbarrier completion) --
+//    a handful of bulk copies per 8 KB instead of 512 16-byte requests; pools
+//    with block_size < 8 use per-lane cp.async into the same layout.  Loads
+//    for the next tiles, also across segment boundaries, are in flight while
+//    the current tile is computed.  No CTA barrier in the main loop.
 //  * Grouped-query packing: the G = Hq/Hkv query heads (times q_len rows)
 //    of a KV head form the N=8*NT columns of a transposed product
 //    S^T = K * Q^T (mma.sync m16n8k16, keys in M), so each KV tile is read
@@ -37,37 +40,58 @@ namespace pa {
 namespace {
 
 constexpr int TILE = 16;
-constexpr int NC_MAX = 16;  // max packed columns (q rows x group heads)
-constexpr int DEC_NW = 4;   // warps per CTA
+constexpr int NC_MAX = 16;      // max packed columns (q rows x group heads)
+constexpr int MAX_NW = 8;       // worker warps per CTA (upper bound)
+constexpr int SMEM_LIMIT = 227 * 1024;
+constexpr int META_B = 16;      // per stage: [0] fp16 half-select mask of the scale words, [1] missing rows
+#ifndef PA_DEC_STAGE_BUDGET
+#define PA_DEC_STAGE_BUDGET (26 * 1024)  // shared-memory bytes of tile ring per warp
+#endif
 
 template <int D, int KVT>
 struct DecCfg {
   static constexpr bool INT8 = KVT == KV_I8;
   static constexpr int ELT = INT8 ? 1 : 2;
-  static constexpr int ROWB = D * ELT;
+  static constexpr int ROWB = D * ELT;                 // bytes of one key row of one head
   static constexpr int CHUNKS = ROWB / 16;
-  static constexpr int TILEB = TILE * ROWB;
-  static constexpr int SCB = INT8 ? 144 : 0;  // 32 scale words + half-select mask (padded)
-  static constexpr int STAGEB = 2 * TILEB + SCB;
-  static constexpr int STAGES_RAW = (32 * 1024) / STAGEB;
+  static constexpr int TILEB = TILE * ROWB;            // K (or V) tile bytes, multiple of 1024
+  static constexpr int HALVES = ROWB >= 128 ? ROWB / 128 : 1;  // TMA boxes across head_dim
+  static constexpr int BOXD = (ROWB >= 128 ? 128 : ROWB) / ELT;
+  static constexpr int SCB = (INT8 ? 128 : 0) + META_B;  // scale words + meta
+  static constexpr int STAGE_RAW = 2 * TILEB + SCB + 8;
+  static constexpr int STAGES_RAW = PA_DEC_STAGE_BUDGET / STAGE_RAW;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int ROWS_PER_IT = 32 / CHUNKS;
   static constexpr int LOAD_ITS = TILE / ROWS_PER_IT;
+  static_assert(TILEB % 1024 == 0, "tiles must keep TMA swizzle atoms aligned");
 };
 
-// Shared-memory chunk swizzles (16-byte units) that make the fragment reads
-// below bank-conflict free.
-template <int D, int KVT>
-__device__ __forceinline__ int swz_k(int row, int c) {
-  if constexpr (KVT != KV_I8) return c ^ (row & 7);
-  else if constexpr (D >= 128) return c ^ ((row & 1) << 2);
-  else return c;
-}
-template <int D, int KVT>
-__device__ __forceinline__ int swz_v(int row, int c) {
-  if constexpr (KVT != KV_I8) return c ^ (row & 7);
-  else if constexpr (D >= 128) return c ^ (((row >> 1) & 3) << 1);
-  else return c ^ ((row >> 1) & 3);
+template <int D, int KVT, int NT>
+struct DecLayout {
+  using C = DecCfg<D, KVT>;
+  static constexpr int S = C::STAGES;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = S * C::TILEB;
+  static constexpr int SC_OFF = 2 * S * C::TILEB;
+  static constexpr int BAR_OFF = SC_OFF + S * C::SCB;
+  static constexpr int P_OFF = (BAR_OFF + S * 8 + 15) & ~15;  // ldmatrix rows need 16-byte alignment
+  static constexpr int PB = TILE * 8 * NT * 2;
+  static constexpr int WARPB = ((P_OFF + PB) + 1023) & ~1023;
+  static_assert(V_OFF % 1024 == 0 && C::TILEB % 1024 == 0, "TMA boxes need 1024-byte aligned tiles");
+  static_assert(SC_OFF % 16 == 0 && C::SCB % 16 == 0, "scale words / meta must stay 16-byte aligned");
+  static_assert(BAR_OFF % 8 == 0, "mbarriers need 8-byte alignment");
+  static_assert(P_OFF % 16 == 0 && WARPB % 1024 == 0, "P buffer / warp regions alignment");
+};
+
+// Byte offset of 16-byte chunk `ch` of key row `row` inside a tile.  This is
+// the layout TMA writes with SWIZZLE_128B (128-byte rows, one 2 KB box per
+// 128 bytes of head_dim) or SWIZZLE_64B (64-byte rows); the cp.async loader
+// writes the same layout.  The XOR makes the ldmatrix / LDS fragment reads
+// bank-conflict free (2-way for INT8 K at D=128).
+template <int ROWB>
+__device__ __forceinline__ int toff(int row, int ch) {
+  if constexpr (ROWB >= 128) return (ch >> 3) * (TILE * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
+  else return row * 64 + ((ch ^ ((row >> 1) & 3)) << 4);
 }
 
 // Query rows of sequence b, never more than the rows Q holds.
@@ -124,15 +148,89 @@ __device__ __forceinline__ void cursor_next(const AttnParams& p, const int* ts, 
   if (c.b < p.B) cursor_seq(p, ts, c);
 }
 
-// Issue the cp.async copies of one tile (K, V, scales) into stage `st`.
+// Scale words of one tile (INT8): lanes 0..15 fetch the K scale of rows
+// 0..15, lanes 16..31 the V scale, each as the aligned 4-byte word holding it;
+// the half-select bits go to the stage meta word 0.
 template <int D, int KVT>
-__device__ __forceinline__ void load_tile(const AttnParams& p, const Cursor& c, unsigned char* st, int lane) {
+__device__ __forceinline__ void load_scales(const AttnParams& p, const Cursor& c, unsigned char* sc, int lane) {
+  const int row = lane & 15;
+  const int key = c.tile * TILE + row;
+  bool ok = key < c.nkeys;
+  int blk = 0, slot = 0;
+  if (ok) {
+    blk = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+    slot = key & (p.BS - 1);
+    ok = blk >= 0 && blk < p.NB;
+  }
+  const bool isv = lane >= 16;
+  unsigned long long addr = reinterpret_cast<unsigned long long>(isv ? p.vs : p.ks);
+  if (ok) {
+    const long long off = isv ? (blk * p.vs_sblk + slot * p.vs_sslot + c.kvh * p.vs_shead)
+                              : (blk * p.ks_sblk + slot * p.ks_sslot + c.kvh * p.ks_shead);
+    addr += static_cast<unsigned long long>(off) * (p.scale_f32 ? 4 : 2);
+  }
+  const unsigned hi = (!p.scale_f32 && ((addr >> 1) & 1)) ? 1u : 0u;
+  const unsigned mask = __ballot_sync(0xffffffffu, hi);
+  cp_async_4(smem_u32(sc) + lane * 4, reinterpret_cast<const void*>(addr & ~3ull), ok ? 4 : 0);
+  if (lane == 0) reinterpret_cast<unsigned*>(sc + 128)[0] = mask;
+}
+
+// TMA fetch of one tile (lane 0): one box of min(16, block_size) slots per
+// block touched and per 128 bytes of head_dim, for K and for V.  Rows that
+// are not fetched (beyond the sequence, or of a block id outside the pool)
+// are recorded in the stage's "missing rows" mask.
+template <int D, int KVT>
+__device__ __forceinline__ void issue_tile_tma(const AttnParams& p, const KvMaps& maps, const Cursor& c,
+                                               uint32_t kdst, uint32_t vdst, uint32_t bar, unsigned* meta) {
+  using C = DecCfg<D, KVT>;
+  const int key0 = c.tile * TILE;
+  const int boxs = p.BS < TILE ? p.BS : TILE;  // 8 or 16 (TMA mode needs block_size >= 8)
+  const int nbox = TILE / boxs;
+  int blks[2] = {-1, -1};
+  int slots[2] = {0, 0};
+  unsigned missing = 0;
+  uint32_t bytes = 0;
+  for (int j = 0; j < nbox; ++j) {
+    const int k = key0 + j * boxs;
+    const unsigned rows = ((1u << boxs) - 1u) << (j * boxs);
+    if (k >= c.nkeys) {
+      missing |= rows;
+      continue;
+    }
+    const int blk = __ldg(c.bt_row + static_cast<long long>(k >> p.log2BS) * p.bt_sc);
+    if (blk < 0 || blk >= p.NB) {
+      set_status(p.status, ST_BAD_BLOCK_ID);
+      missing |= rows;
+      continue;
+    }
+    blks[j] = blk;
+    slots[j] = k & (p.BS - 1);
+    bytes += 2u * C::HALVES * boxs * (C::ROWB >= 128 ? 128 : C::ROWB);
+  }
+  const int valid = c.nkeys - key0;
+  if (valid < TILE) missing |= 0xffffu & ~((1u << (valid > 0 ? valid : 0)) - 1u);
+  meta[1] = missing;
+  mbar_arrive_expect_tx(bar, bytes);
+  for (int j = 0; j < nbox; ++j) {
+    if (blks[j] < 0) continue;
+#pragma unroll
+    for (int h = 0; h < C::HALVES; ++h) {
+      const uint32_t off = h * (TILE * 128) + j * boxs * (C::ROWB >= 128 ? 128 : C::ROWB);
+      tma_load_4d(kdst + off, &maps.k, bar, h * C::BOXD, c.kvh, slots[j], blks[j]);
+      tma_load_4d(vdst + off, &maps.v, bar, h * C::BOXD, c.kvh, slots[j], blks[j]);
+    }
+  }
+}
+
+// cp.async fetch of one tile (all lanes), for pools TMA boxes cannot cover
+// (block_size < 8).  Missing rows are zero-filled.
+template <int D, int KVT>
+__device__ __forceinline__ void issue_tile_cpasync(const AttnParams& p, const Cursor& c, uint32_t kdst,
+                                                   uint32_t vdst, unsigned* meta, int lane) {
   using C = DecCfg<D, KVT>;
   const int key0 = c.tile * TILE;
   const char* kbase = static_cast<const char*>(p.k);
   const char* vbase = static_cast<const char*>(p.v);
-  const uint32_t sk = smem_u32(st);
-  const uint32_t sv = sk + C::TILEB;
   const int ch = lane % C::CHUNKS;
 #pragma unroll
   for (int it = 0; it < C::LOAD_ITS; ++it) {
@@ -154,34 +252,10 @@ __device__ __forceinline__ void load_tile(const AttnParams& p, const Cursor& c, 
       ksrc = kbase + (blk * p.k_sblk + slot * p.k_sslot + c.kvh * p.k_shead) * C::ELT + ch * 16;
       vsrc = vbase + (blk * p.v_sblk + slot * p.v_sslot + c.kvh * p.v_shead) * C::ELT + ch * 16;
     }
-    cp_async_16(sk + row * C::ROWB + swz_k<D, KVT>(row, ch) * 16, ksrc, ok ? 16 : 0);
-    cp_async_16(sv + row * C::ROWB + swz_v<D, KVT>(row, ch) * 16, vsrc, ok ? 16 : 0);
+    cp_async_16(kdst + toff<C::ROWB>(row, ch), ksrc, ok ? 16 : 0);
+    cp_async_16(vdst + toff<C::ROWB>(row, ch), vsrc, ok ? 16 : 0);
   }
-  if constexpr (C::INT8) {
-    // lanes 0..15: K scale of rows 0..15, lanes 16..31: V scale.
-    const int row = lane & 15;
-    const int key = key0 + row;
-    bool ok = key < c.nkeys;
-    int blk = 0, slot = 0;
-    if (ok) {
-      blk = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
-      slot = key & (p.BS - 1);
-      ok = blk >= 0 && blk < p.NB;
-    }
-    const bool isv = lane >= 16;
-    const char* sbase = static_cast<const char*>(isv ? p.vs : p.ks);
-    unsigned long long addr = reinterpret_cast<unsigned long long>(sbase);
-    if (ok) {
-      const long long off = isv ? (blk * p.vs_sblk + slot * p.vs_sslot + c.kvh * p.vs_shead)
-                                : (blk * p.ks_sblk + slot * p.ks_sslot + c.kvh * p.ks_shead);
-      addr += static_cast<unsigned long long>(off) * (p.scale_f32 ? 4 : 2);
-    }
-    const unsigned hi = (!p.scale_f32 && ((addr >> 1) & 1)) ? 1u : 0u;
-    const unsigned mask = __ballot_sync(0xffffffffu, hi);
-    const uint32_t ss = sv + C::TILEB;
-    cp_async_4(ss + lane * 4, reinterpret_cast<const void*>(addr & ~3ull), ok ? 4 : 0);
-    if (lane == 0) *reinterpret_cast<unsigned*>(st + 2 * C::TILEB + 128) = mask;
-  }
+  if (lane == 0) meta[1] = 0u;
 }
 
 __device__ __forceinline__ float scale_from_word(uint32_t w, bool hi, int is_f32) {
@@ -190,31 +264,43 @@ __device__ __forceinline__ float scale_from_word(uint32_t w, bool hi, int is_f32
   return __half2float(__ushort_as_half(h));
 }
 
-template <int D, int KVT, int QT, int NT, int STAGES>
-__global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnParams p) {
+template <int D, int KVT, int QT, int NT, bool TMA>
+__global__ void __launch_bounds__(MAX_NW * 32, 1)
+    pa_decode_kernel(const AttnParams p, const __grid_constant__ KvMaps maps) {
   using C = DecCfg<D, KVT>;
+  using Lay = DecLayout<D, KVT, NT>;
+  constexpr int STAGES = C::STAGES;
   constexpr bool INT8 = C::INT8;
   constexpr bool MMA_BF16 = (KVT == KV_BF16);
   constexpr bool QIS_BF16 = (QT == Q_BF16);
+  constexpr bool USE_CPASYNC = !TMA || INT8;  // cp.async carries tiles (no TMA) or scale words (INT8)
   constexpr int KS = D / 16;  // k-steps over head_dim / m-tiles of O^T
   constexpr int NC = 8 * NT;
-  constexpr int PB = TILE * NC * 2;
-  constexpr int WARPB = STAGES * C::STAGEB + PB;
 
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  int* s_ts = reinterpret_cast<int*>(smem);
+  const int NW = blockDim.x >> 5;
+  int* s_ts = reinterpret_cast<int*>(smem_raw);
   const int ts_bytes = ((p.B + 1) * 4 + 127) & ~127;
-  unsigned char* wsm = smem + ts_bytes + warp * WARPB;
-  unsigned char* pbuf = wsm + STAGES * C::STAGEB;
+  // warp regions start on a 1024-byte boundary (TMA swizzle atoms)
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t wbase_u32 = ((raw_u32 + ts_bytes + 1023) & ~1023u) + warp * Lay::WARPB;
+  unsigned char* wsm = smem_raw + (wbase_u32 - raw_u32);
+  unsigned char* pbuf = wsm + Lay::P_OFF;
 
   // ---- prologue: tiles per sequence and their exclusive scan -------------
-  for (int i = tid; i < p.B; i += DEC_NW * 32) {
+  for (int i = tid; i < p.B; i += NW * 32) {
     const int nk = seq_keys(p, i);
     if (p.nblk[i] > p.bt_cols) set_status(p.status, ST_BAD_NUM_BLOCKS);
     s_ts[i] = (nk + TILE - 1) / TILE;
+  }
+  if constexpr (TMA) {
+    if (lane == 0) {
+      for (int s = 0; s < STAGES; ++s) mbar_init(wbase_u32 + Lay::BAR_OFF + 8 * s, 1);
+      fence_mbar_init();
+    }
   }
   __syncthreads();
   if (warp == 0) {
@@ -235,13 +321,13 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
   }
   __syncthreads();
   if (blockIdx.x == 0) {
-    for (int i = tid; i <= p.B; i += DEC_NW * 32) p.tstart[i] = s_ts[i];
+    for (int i = tid; i <= p.B; i += NW * 32) p.tstart[i] = s_ts[i];
   }
 
   const int total = s_ts[p.B] * p.Hkv;
   const int W = p.num_warps_total;
   const int chunk = (total + W - 1) / W;
-  const int gw = blockIdx.x * DEC_NW + warp;
+  const int gw = blockIdx.x * NW + warp;
   const int g0 = gw * chunk;
   const int g1 = min(g0 + chunk, total);
   if (total == 0 || g0 >= g1) return;
@@ -253,13 +339,26 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
   cursor_locate(p, s_ts, g0, ld);
   cp = ld;
 
+  auto issue = [&](int slot_idx) {
+    const uint32_t kdst = wbase_u32 + Lay::K_OFF + slot_idx * C::TILEB;
+    const uint32_t vdst = wbase_u32 + Lay::V_OFF + slot_idx * C::TILEB;
+    unsigned char* sc = wsm + Lay::SC_OFF + slot_idx * C::SCB;
+    unsigned* meta = reinterpret_cast<unsigned*>(sc + (INT8 ? 128 : 0));
+    if constexpr (TMA) {
+      if (lane == 0) issue_tile_tma<D, KVT>(p, maps, ld, kdst, vdst, wbase_u32 + Lay::BAR_OFF + 8 * slot_idx, meta);
+    } else {
+      issue_tile_cpasync<D, KVT>(p, ld, kdst, vdst, meta, lane);
+    }
+    if constexpr (INT8) load_scales<D, KVT>(p, ld, sc, lane);
+  };
+
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
     if (g0 + s < g1) {
-      load_tile<D, KVT>(p, ld, wsm + s * C::STAGEB, lane);
+      issue(s);
       cursor_next(p, s_ts, ld);
     }
-    cp_async_commit();
+    if constexpr (USE_CPASYNC) cp_async_commit();
   }
 
   uint32_t qf[NT][KS][2];
@@ -268,16 +367,20 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
   int lim[NT][2];
   int piece_start_tile = 0;
   bool piece_first = true;  // first piece of this warp's range
+  bool zeroed_prev = false;
 
   for (int g = g0; g < g1; ++g) {
     const int i = g - g0;
     // ---- prefetch tile i + STAGES - 1 into the slot freed last iteration --
+    if constexpr (TMA) {
+      if (zeroed_prev) fence_proxy_async_smem();  // generic zero-fill before the next TMA write
+    }
     __syncwarp();
     if (g + STAGES - 1 < g1) {
-      load_tile<D, KVT>(p, ld, wsm + ((i + STAGES - 1) % STAGES) * C::STAGEB, lane);
+      issue((i + STAGES - 1) % STAGES);
       cursor_next(p, s_ts, ld);
     }
-    cp_async_commit();
+    if constexpr (USE_CPASYNC) cp_async_commit();
 
     const bool pstart = (g == g0) || (cp.tile == 0);
     const bool pend = (g == g1 - 1) || (cp.tile == cp.nt - 1);
@@ -345,11 +448,33 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
     }
 
     // ---- wait for this tile ----------------------------------------------
-    cp_async_wait<STAGES - 1>();
+    const int slot_idx = i % STAGES;
+    if constexpr (USE_CPASYNC) cp_async_wait<STAGES - 1>();
+    if constexpr (TMA) {
+      if (!mbar_wait(wbase_u32 + Lay::BAR_OFF + 8 * slot_idx, (i / STAGES) & 1) && lane == 0)
+        set_status(p.status, ST_WAIT_TIMEOUT);
+    }
     __syncwarp();
-    unsigned char* st = wsm + (i % STAGES) * C::STAGEB;
-    const uint32_t sk = smem_u32(st);
-    const uint32_t sv = sk + C::TILEB;
+    unsigned char* kt = wsm + Lay::K_OFF + slot_idx * C::TILEB;
+    unsigned char* vt = wsm + Lay::V_OFF + slot_idx * C::TILEB;
+    unsigned char* sc = wsm + Lay::SC_OFF + slot_idx * C::SCB;
+    const uint32_t sk = smem_u32(kt);
+    const uint32_t sv = smem_u32(vt);
+    zeroed_prev = false;
+    if constexpr (TMA && !INT8) {
+      // rows not fetched (or past the sequence) may hold stale or non-finite
+      // bytes: zero them in V so that P = 0 really contributes nothing.
+      const unsigned missing = reinterpret_cast<const unsigned*>(sc)[1];
+      if (missing) {
+        for (int idx = lane; idx < TILE * C::CHUNKS; idx += 32) {
+          const int row = idx / C::CHUNKS;
+          if ((missing >> row) & 1u)
+            *reinterpret_cast<uint4*>(vt + toff<C::ROWB>(row, idx % C::CHUNKS)) = make_uint4(0, 0, 0, 0);
+        }
+        zeroed_prev = true;
+        __syncwarp();
+      }
+    }
 
     // ---- S^T = K * Q^T -----------------------------------------------------
     float s[NT][4];
@@ -363,8 +488,7 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
 #pragma unroll
       for (int kk = 0; kk < KS; ++kk) {
         uint32_t a[4];
-        const int chn = 2 * kk + (j >> 1);
-        ldsm_x4(sk + row * C::ROWB + swz_k<D, KVT>(row, chn) * 16, a[0], a[1], a[2], a[3]);
+        ldsm_x4(sk + toff<C::ROWB>(row, 2 * kk + (j >> 1)), a[0], a[1], a[2], a[3]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(s[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
       }
@@ -372,9 +496,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
 #pragma unroll
       for (int gg = 0; gg < D / 64; ++gg) {
         const int chn = 4 * gg + q4;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(st + r * C::ROWB + swz_k<D, KVT>(r, chn) * 16);
-        const uint4 w1 =
-            *reinterpret_cast<const uint4*>(st + (r + 8) * C::ROWB + swz_k<D, KVT>(r + 8, chn) * 16);
+        const uint4 w0 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB>(r, chn));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB>(r + 8, chn));
         const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w};
         const uint32_t x1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
@@ -391,8 +514,8 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
     // ---- scales (INT8) --------------------------------------------------
     float ksc0 = 1.f, ksc1 = 1.f, vsc0 = 1.f, vsc1 = 1.f;
     if constexpr (INT8) {
-      const uint32_t* sw = reinterpret_cast<const uint32_t*>(st + 2 * C::TILEB);
-      const unsigned hm = *reinterpret_cast<const unsigned*>(st + 2 * C::TILEB + 128);
+      const uint32_t* sw = reinterpret_cast<const uint32_t*>(sc);
+      const unsigned hm = reinterpret_cast<const unsigned*>(sc + 128)[0];
       ksc0 = scale_from_word(sw[r], (hm >> r) & 1, p.scale_f32);
       ksc1 = scale_from_word(sw[r + 8], (hm >> (r + 8)) & 1, p.scale_f32);
       vsc0 = scale_from_word(sw[16 + r], (hm >> (16 + r)) & 1, p.scale_f32);
@@ -455,27 +578,24 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
 #pragma unroll
       for (int mt = 0; mt < KS; ++mt) {
         uint32_t a[4];
-        const int chn = 2 * mt + (j & 1);
-        ldsm_x4_t(sv + row * C::ROWB + swz_v<D, KVT>(row, chn) * 16, a[0], a[1], a[2], a[3]);
+        ldsm_x4_t(sv + toff<C::ROWB>(row, 2 * mt + (j & 1)), a[0], a[1], a[2], a[3]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(acc[mt][nt], a, bp[nt][0], bp[nt][1]);
       }
     } else {
-      const unsigned char* vt = st + C::TILEB;
       constexpr int WORDS = D / 32;  // 32-bit words of this thread's d range per key
       uint32_t R[4][WORDS];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int row = 2 * q4 + (c & 1) + 8 * (c >> 1);
         if constexpr (D >= 128) {
-          const uint4 w = *reinterpret_cast<const uint4*>(vt + row * C::ROWB + swz_v<D, KVT>(row, r) * 16);
+          const uint4 w = *reinterpret_cast<const uint4*>(vt + toff<C::ROWB>(row, r));
           R[c][0] = w.x;
           R[c][1] = w.y;
           R[c][2] = w.z;
           R[c][3] = w.w;
         } else {
-          const uint2 w = *reinterpret_cast<const uint2*>(vt + row * C::ROWB + swz_v<D, KVT>(row, r >> 1) * 16 +
-                                                          (r & 1) * 8);
+          const uint2 w = *reinterpret_cast<const uint2*>(vt + toff<C::ROWB>(row, r >> 1) + (r & 1) * 8);
           R[c][0] = w.x;
           R[c][1] = w.y;
         }
@@ -551,7 +671,7 @@ __global__ void __launch_bounds__(DEC_NW * 32, 1) pa_decode_kernel(const AttnPar
     }
     cursor_next(p, s_ts, cp);
   }
-  cp_async_wait<0>();
+  if constexpr (USE_CPASYNC) cp_async_wait<0>();
 }
 
 // Combine the split-K partials of every segment that straddles warp ranges.
@@ -621,29 +741,35 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
   }
 }
 
-template <int D, int KVT, int QT, int NT>
+template <int D, int KVT, int QT, int NT, bool TMA>
 struct DecodeInst {
-  using C = DecCfg<D, KVT>;
-  static constexpr int STAGES = C::STAGES;
-  static constexpr int WARPB = STAGES * C::STAGEB + TILE * 8 * NT * 2;
-  static size_t smem_bytes(int B) { return static_cast<size_t>(((B + 1) * 4 + 127) & ~127) + DEC_NW * WARPB; }
-  static int grid(int B) {
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    auto kern = pa_decode_kernel<D, KVT, QT, NT, STAGES>;
-    const size_t sm = smem_bytes(B);
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DEC_NW * 32, sm);
+  using Lay = DecLayout<D, KVT, NT>;
+  static int plan(int B, DecodeLaunch* out) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    const int ts_bytes = ((B + 1) * 4 + 127) & ~127;
+    const int fixed = ts_bytes + 1024;  // scan + alignment slack
+    int nw = (SMEM_LIMIT - fixed) / Lay::WARPB;
+    if (nw > MAX_NW) nw = MAX_NW;
+    if (nw < 1) return -1;
+    out->warps_per_cta = nw;
+    out->smem = static_cast<size_t>(fixed + nw * Lay::WARPB);
+    auto kern = pa_decode_kernel<D, KVT, QT, NT, TMA>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(out->smem)) !=
+        cudaSuccess)
+      return -1;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nw * 32, out->smem);
     if (per_sm < 1) per_sm = 1;
-    return sms * per_sm;
+    out->ctas = sms * per_sm;
+    return 0;
   }
-  static cudaError_t launch(const AttnParams& p, cudaStream_t stream, int grid_ctas) {
-    auto kern = pa_decode_kernel<D, KVT, QT, NT, STAGES>;
-    const size_t sm = smem_bytes(p.B);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  static cudaError_t launch(const AttnParams& p, const KvMaps& maps, const DecodeLaunch& pl, cudaStream_t stream) {
+    auto kern = pa_decode_kernel<D, KVT, QT, NT, TMA>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
     if (e != cudaSuccess) return e;
-    kern<<<grid_ctas, DEC_NW * 32, sm, stream>>>(p);
+    kern<<<pl.ctas, pl.warps_per_cta * 32, pl.smem, stream>>>(p, maps);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     pa_decode_merge_kernel<D><<<dim3(p.Hkv, p.B), 128, 0, stream>>>(p);
@@ -652,39 +778,50 @@ struct DecodeInst {
 };
 
 template <int D, int KVT, int QT>
-int grid_nt(int nt, int B) {
-  return nt == 1 ? DecodeInst<D, KVT, QT, 1>::grid(B) : DecodeInst<D, KVT, QT, 2>::grid(B);
-}
-template <int D, int KVT, int QT>
-cudaError_t launch_nt(const AttnParams& p, int nt, int grid, cudaStream_t s) {
-  return nt == 1 ? DecodeInst<D, KVT, QT, 1>::launch(p, s, grid) : DecodeInst<D, KVT, QT, 2>::launch(p, s, grid);
+struct Sel {
+  static int plan(int nt, int B, bool tma, DecodeLaunch* o) {
+    if (nt == 1) return tma ? DecodeInst<D, KVT, QT, 1, true>::plan(B, o) : DecodeInst<D, KVT, QT, 1, false>::plan(B, o);
+    return tma ? DecodeInst<D, KVT, QT, 2, true>::plan(B, o) : DecodeInst<D, KVT, QT, 2, false>::plan(B, o);
+  }
+  static cudaError_t launch(const AttnParams& p, const KvMaps& m, int nt, bool tma, const DecodeLaunch& pl,
+                            cudaStream_t s) {
+    if (nt == 1)
+      return tma ? DecodeInst<D, KVT, QT, 1, true>::launch(p, m, pl, s) : DecodeInst<D, KVT, QT, 1, false>::launch(p, m, pl, s);
+    return tma ? DecodeInst<D, KVT, QT, 2, true>::launch(p, m, pl, s) : DecodeInst<D, KVT, QT, 2, false>::launch(p, m, pl, s);
+  }
+};
+
+template <int D>
+int plan_kv(int kv, int qbf, int nt, int B, bool tma, DecodeLaunch* o) {
+  if (kv == KV_F16) return qbf ? Sel<D, KV_F16, Q_BF16>::plan(nt, B, tma, o) : Sel<D, KV_F16, Q_F16>::plan(nt, B, tma, o);
+  if (kv == KV_BF16) return qbf ? Sel<D, KV_BF16, Q_BF16>::plan(nt, B, tma, o) : Sel<D, KV_BF16, Q_F16>::plan(nt, B, tma, o);
+  return qbf ? Sel<D, KV_I8, Q_BF16>::plan(nt, B, tma, o) : Sel<D, KV_I8, Q_F16>::plan(nt, B, tma, o);
 }
 template <int D>
-int grid_kv(int kv, int qbf, int nt, int B) {
-  if (kv == KV_F16) return qbf ? grid_nt<D, KV_F16, Q_BF16>(nt, B) : grid_nt<D, KV_F16, Q_F16>(nt, B);
-  if (kv == KV_BF16) return qbf ? grid_nt<D, KV_BF16, Q_BF16>(nt, B) : grid_nt<D, KV_BF16, Q_F16>(nt, B);
-  return qbf ? grid_nt<D, KV_I8, Q_BF16>(nt, B) : grid_nt<D, KV_I8, Q_F16>(nt, B);
-}
-template <int D>
-cudaError_t launch_kv(const AttnParams& p, int kv, int qbf, int nt, int grid, cudaStream_t s) {
-  if (kv == KV_F16) return qbf ? launch_nt<D, KV_F16, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_F16, Q_F16>(p, nt, grid, s);
-  if (kv == KV_BF16) return qbf ? launch_nt<D, KV_BF16, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_BF16, Q_F16>(p, nt, grid, s);
-  return qbf ? launch_nt<D, KV_I8, Q_BF16>(p, nt, grid, s) : launch_nt<D, KV_I8, Q_F16>(p, nt, grid, s);
+cudaError_t launch_kv(const AttnParams& p, const KvMaps& m, int kv, int qbf, int nt, bool tma, const DecodeLaunch& pl,
+                      cudaStream_t s) {
+  if (kv == KV_F16)
+    return qbf ? Sel<D, KV_F16, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_F16, Q_F16>::launch(p, m, nt, tma, pl, s);
+  if (kv == KV_BF16)
+    return qbf ? Sel<D, KV_BF16, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_BF16, Q_F16>::launch(p, m, nt, tma, pl, s);
+  return qbf ? Sel<D, KV_I8, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_I8, Q_F16>::launch(p, m, nt, tma, pl, s);
 }
 
 }  // namespace
 
-int decode_warps_per_cta() { return DEC_NW; }
-
-int decode_grid_size(int kv_kind, int q_bf16, int D, int nt, int B) {
-  if (D == 64) return grid_kv<64>(kv_kind, q_bf16, nt, B);
-  if (D == 128) return grid_kv<128>(kv_kind, q_bf16, nt, B);
-  return 0;
+int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, DecodeLaunch* out) {
+  if (D == 64) return plan_kv<64>(kv_kind, q_bf16, nt, B, use_tma != 0, out);
+  if (D == 128) return plan_kv<128>(kv_kind, q_bf16, nt, B, use_tma != 0, out);
+  return -1;
 }
 
-cudaError_t launch_decode(const AttnParams& p, int kv_kind, int q_bf16, int D, int nt, int grid, cudaStream_t stream) {
-  if (D == 64) return launch_kv<64>(p, kv_kind, q_bf16, nt, grid, stream);
-  if (D == 128) return launch_kv<128>(p, kv_kind, q_bf16, nt, grid, stream);
+cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
+                          const DecodeLaunch& plan, cudaStream_t stream) {
+  KvMaps none{};
+  const KvMaps& m = maps ? *maps : none;
+  const bool tma = maps != nullptr;
+  if (D == 64) return launch_kv<64>(p, m, kv_kind, q_bf16, nt, tma, plan, stream);
+  if (D == 128) return launch_kv<128>(p, m, kv_kind, q_bf16, nt, tma, plan, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "paged_attn_b200.h"
@@ -19,6 +20,13 @@ enum : int {
   ST_BAD_POSITION = 2,     // write position beyond the block table row
   ST_BAD_NUM_BLOCKS = 4,   // num_blocks_per_seq larger than the block table width
   ST_BAD_SEQ_INDEX = 8,    // token -> sequence index outside [0, num_seqs)
+  ST_WAIT_TIMEOUT = 16,    // a bounded wait on an asynchronous copy gave up
+};
+
+// TMA descriptors of the K and V pools (4-D maps over [block, slot, head, d]).
+struct alignas(64) KvMaps {
+  CUtensorMap k;
+  CUtensorMap v;
 };
 
 struct AttnParams {
@@ -91,10 +99,15 @@ struct WriteParams {
 cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream);
 // Decode: persistent grid size (CTAs) for a configuration on the current
 // device, warps per CTA, and the launch of the split kernel + merge kernel.
-int decode_grid_size(int kv_kind, int q_bf16, int D, int nt, int B);
-int decode_warps_per_cta();
-cudaError_t launch_decode(const AttnParams& p, int kv_kind, int q_bf16, int D, int nt, int grid,
-                          cudaStream_t stream);
+struct DecodeLaunch {
+  int ctas;           // persistent CTAs
+  int warps_per_cta;  // worker warps per CTA
+  size_t smem;        // dynamic shared memory per CTA
+};
+// use_tma: the pool can be read with TMA boxes (block_size >= 8, maps built).
+int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, DecodeLaunch* out);
+cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
+                          const DecodeLaunch& plan, cudaStream_t stream);
 cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);
 
 }  // namespace pa
