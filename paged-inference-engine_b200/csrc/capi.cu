@@ -229,9 +229,13 @@ bool make_pool_map(CUtensorMap* m, void* base, int dtype, int D, int H, int BS, 
                                  static_cast<cuuint64_t>(s_blk * elt)};
   const cuuint32_t box[4] = {boxd, 1, static_cast<cuuint32_t>(BS < 16 ? BS : 16), 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
+  // L2 fills no wider than one box row: a wider promotion drags the next
+  // head's row of the same slot out of DRAM with every row.
+  const CUtensorMapL2promotion l2 = rowb >= 256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                                    : rowb >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                                  : CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
   const CUresult r = enc(m, elt == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, base, dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

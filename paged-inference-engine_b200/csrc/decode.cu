@@ -41,11 +41,18 @@ namespace {
 
 constexpr int TILE = 16;
 constexpr int NC_MAX = 16;      // max packed columns (q rows x group heads)
-constexpr int MAX_NW = 8;       // worker warps per CTA (upper bound)
+// Worker warps per CTA (upper bound): 12 for single-n-tile variants (<= 170
+// registers per thread), 8 for the two-n-tile ones.
+template <int NT>
+constexpr int max_warps() { return NT == 1 ? 12 : 8; }
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int META_B = 16;      // per stage: [0] fp16 half-select mask of the scale words, [1] missing rows
+// Shared-memory bytes of tile ring per warp (16-bit pools / int8 pools).
 #ifndef PA_DEC_STAGE_BUDGET
-#define PA_DEC_STAGE_BUDGET (26 * 1024)  // shared-memory bytes of tile ring per warp
+#define PA_DEC_STAGE_BUDGET (26 * 1024)
+#endif
+#ifndef PA_DEC_STAGE_BUDGET_I8
+#define PA_DEC_STAGE_BUDGET_I8 (17 * 1024)
 #endif
 
 template <int D, int KVT>
@@ -59,7 +66,7 @@ struct DecCfg {
   static constexpr int BOXD = (ROWB >= 128 ? 128 : ROWB) / ELT;
   static constexpr int SCB = (INT8 ? 128 : 0) + META_B;  // scale words + meta
   static constexpr int STAGE_RAW = 2 * TILEB + SCB + 8;
-  static constexpr int STAGES_RAW = PA_DEC_STAGE_BUDGET / STAGE_RAW;
+  static constexpr int STAGES_RAW = (INT8 ? PA_DEC_STAGE_BUDGET_I8 : PA_DEC_STAGE_BUDGET) / STAGE_RAW;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int ROWS_PER_IT = 32 / CHUNKS;
   static constexpr int LOAD_ITS = TILE / ROWS_PER_IT;
@@ -265,7 +272,7 @@ __device__ __forceinline__ float scale_from_word(uint32_t w, bool hi, int is_f32
 }
 
 template <int D, int KVT, int QT, int NT, bool TMA>
-__global__ void __launch_bounds__(MAX_NW * 32, 1)
+__global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
     pa_decode_kernel(const AttnParams p, const __grid_constant__ KvMaps maps) {
   using C = DecCfg<D, KVT>;
   using Lay = DecLayout<D, KVT, NT>;
@@ -366,6 +373,7 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
   float m_run[NT][2], l_run[NT][2];
   int lim[NT][2];
   int piece_start_tile = 0;
+  int qlen_b = 0;
   bool piece_first = true;  // first piece of this warp's range
   bool zeroed_prev = false;
 
@@ -384,8 +392,8 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
 
     const bool pstart = (g == g0) || (cp.tile == 0);
     const bool pend = (g == g1 - 1) || (cp.tile == cp.nt - 1);
-    const int qlen_b = seq_qlen(p, cp.b);
     if (pstart) {
+      qlen_b = seq_qlen(p, cp.b);
       piece_start_tile = cp.tile;
       // ---- Q^T fragments of the packed (q row, group head) columns -------
       const int off = p.top_left ? 0 : (p.kvlen[cp.b] - qlen_b);
@@ -483,6 +491,12 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) s[nt][c] = 0.f;
     if constexpr (!INT8) {
+      // two independent accumulation chains halve the dependent-MMA latency
+      float s2[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s2[nt][c] = 0.f;
       const int j = lane >> 3;
       const int row = (lane & 7) + 8 * (j & 1);
 #pragma unroll
@@ -490,9 +504,21 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
         uint32_t a[4];
         ldsm_x4(sk + toff<C::ROWB>(row, 2 * kk + (j >> 1)), a[0], a[1], a[2], a[3]);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(s[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          if (kk & 1) mma16816<MMA_BF16>(s2[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+          else mma16816<MMA_BF16>(s[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+        }
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[nt][c] += s2[nt][c];
     } else {
+      float s2[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s2[nt][c] = 0.f;
 #pragma unroll
       for (int gg = 0; gg < D / 64; ++gg) {
         const int chn = 4 * gg + q4;
@@ -506,9 +532,16 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
           i8x4_to_f16x4(x0[jj], a[0], a[2]);
           i8x4_to_f16x4(x1[jj], a[1], a[3]);
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma16816<false>(s[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+          for (int nt = 0; nt < NT; ++nt) {
+            if (jj & 1) mma16816<false>(s2[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+            else mma16816<false>(s[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+          }
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[nt][c] += s2[nt][c];
     }
 
     // ---- scales (INT8) --------------------------------------------------
@@ -547,12 +580,15 @@ __global__ void __launch_bounds__(MAX_NW * 32, 1)
         pv[e] = p0;
         pv[2 + e] = p1;
       }
+      // alpha == 1 for every column of the warp: the running max did not move
+      if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
 #pragma unroll
-      for (int mt = 0; mt < KS; ++mt) {
-        acc[mt][nt][0] *= alpha[0];
-        acc[mt][nt][1] *= alpha[1];
-        acc[mt][nt][2] *= alpha[0];
-        acc[mt][nt][3] *= alpha[1];
+        for (int mt = 0; mt < KS; ++mt) {
+          acc[mt][nt][0] *= alpha[0];
+          acc[mt][nt][1] *= alpha[1];
+          acc[mt][nt][2] *= alpha[0];
+          acc[mt][nt][3] *= alpha[1];
+        }
       }
       // P^T tile [key][col] (fp16 or bf16, V scale folded in for INT8)
       pw[(r * NC + nt * 8 + 2 * q4) >> 1] = pack2<MMA_BF16>(pv[0] * vsc0, pv[1] * vsc0);
@@ -751,7 +787,7 @@ struct DecodeInst {
     const int ts_bytes = ((B + 1) * 4 + 127) & ~127;
     const int fixed = ts_bytes + 1024;  // scan + alignment slack
     int nw = (SMEM_LIMIT - fixed) / Lay::WARPB;
-    if (nw > MAX_NW) nw = MAX_NW;
+    if (nw > max_warps<NT>()) nw = max_warps<NT>();
     if (nw < 1) return -1;
     out->warps_per_cta = nw;
     out->smem = static_cast<size_t>(fixed + nw * Lay::WARPB);
