@@ -184,6 +184,27 @@ int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
                       size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * paged_attn_decode without a caller-supplied workspace.  It has no
+ * counterpart in the reference.  It is meant for callers that cannot allocate
+ * device memory per call: a serving engine that has pre-reserved all of HBM for
+ * its KV pool and owns the only allocator, or a host binding (JNI, cgo, a
+ * plugin ABI) that has pointers to tensors but no allocator of its own.
+ * The split-K partials live in one 24 MiB static device array inside this
+ * library, which every GPU that loads the library keeps until the process
+ * exits.  Limits: num_seqs <= 8192 and max_q_len * (num_q_heads / num_kv_heads)
+ * <= 16 (PA_ERR_UNSUPPORTED otherwise); when the partials of the full
+ * persistent grid would not fit, fewer warps per CTA are launched.
+ * The first call on each device looks up the array's device address (and may
+ * load the library's GPU module), so make that first call before any stream
+ * capture.  All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller.  The array
+ * keeps the last call's contents; nothing in it needs to start at zero because
+ * every call writes each partial before it reads it.
+ */
+int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg,
+                              int32_t* status, void* stream);
+
+/*
  * Tiled causal paged attention for long query blocks (prefill / chunked
  * prefill): the q_len > 1 grid of kernels/flash_attention.py:19-136.
  */

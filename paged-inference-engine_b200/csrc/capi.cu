@@ -359,6 +359,39 @@ int build_write(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_
   return PA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Split-K scratch for paged_attn_decode_noalloc: a fixed array that every GPU
+// loading this library holds in device memory until the process exits, so the
+// entry point never allocates.  Host code cannot use the symbol's name as a
+// device address (on the host it names a shadow variable), so the address is
+// looked up once per device with cudaGetSymbolAddress while that device is
+// current.
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = static_cast<size_t>(24) << 20;  // 24 MiB per device
+static __device__ __align__(256) unsigned char g_decode_scratch[kStaticScratchBytes];
+
+// Device address of g_decode_scratch on the current device (set up on first
+// use per device).
+int static_scratch_address(void** out) {
+  static std::mutex mu;
+  static std::map<int, void*> addr;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = addr.find(dev);
+  if (it != addr.end()) {
+    *out = it->second;
+    return PA_OK;
+  }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_decode_scratch);
+  if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(decode scratch)");
+  addr[dev] = p;
+  *out = p;
+  return PA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -430,6 +463,53 @@ int kv_write_copy(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_pagin
   if (kv->dtype == PA_DTYPE_I8) return fail(PA_ERR_INVALID, "kv_write_copy needs an fp16 / bf16 pool");
   cudaError_t e = pa::launch_kv_write(w, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "kv_write_copy launch");
+  return PA_OK;
+}
+
+// Decode with the split-K scratch taken from the library's own static device
+// array (see paged_attn_b200.h).  The persistent grid keeps every SM but may use
+// fewer warps per CTA so that the partials fit the fixed scratch.
+int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg,
+                              int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  if (p.B > kMaxDecodeSeqs)
+    return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc) supports at most %d sequences per call", kMaxDecodeSeqs);
+  if (p.maxq * p.G > kNcMax)
+    return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc) packs at most %d (q rows x group heads) columns", kNcMax);
+  if (p.B == 0 || p.maxq == 0) return PA_OK;
+  void* scratch = nullptr;
+  rc = static_scratch_address(&scratch);
+  if (rc) return rc;
+  const int nt = decode_nt(p);
+  const int kv_k = kv_kind(kv->dtype);
+  pa::KvMaps maps;
+  const bool tma = make_kv_maps(kv, &maps);
+  pa::DecodeLaunch plan;
+  if (cached_plan(kv_k, p.q_bf16, kv->head_dim, nt, p.B, tma, &plan) != 0)
+    return fail(PA_ERR_CUDA, "could not plan the decode launch (no CUDA device?)");
+  // dynamic shared memory = fixed part + warps * per-warp ring
+  const size_t fixed = static_cast<size_t>(((p.B + 1) * 4 + 127) & ~127) + 1024;
+  const size_t warp_bytes = (plan.smem - fixed) / plan.warps_per_cta;
+  int nw = plan.warps_per_cta;
+  while (nw > 0 && ws_layout(plan.ctas * nw, kv->head_dim, p.B).total > kStaticScratchBytes) --nw;
+  if (nw < 1)
+    return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc): %d CTAs x 1 warp need more than the %zu-byte static scratch",
+                plan.ctas, kStaticScratchBytes);
+  const WsLayout L = ws_layout(plan.ctas * nw, kv->head_dim, p.B);
+  char* base = static_cast<char*>(scratch);
+  p.part_o = reinterpret_cast<float*>(base + L.part_o);
+  p.part_ml = reinterpret_cast<float*>(base + L.part_ml);
+  p.tstart = reinterpret_cast<int*>(base + L.tstart);
+  p.num_warps_total = plan.ctas * nw;
+  pa::DecodeLaunch pl = plan;
+  pl.warps_per_cta = nw;
+  pl.smem = fixed + nw * warp_bytes;
+  cudaError_t e = pa::launch_decode(p, tma ? &maps : nullptr, kv_k, p.q_bf16, kv->head_dim, nt, pl,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode (no-alloc) launch");
   return PA_OK;
 }
 
