@@ -169,7 +169,7 @@ def paged_attention(q, k_pool, v_pool, q_len, block_table, num_blocks, block_siz
             continue
         kseq = torch.from_numpy(gather_sequence(k_pool, k_scale, block_table[b], nk))  # [nk, Hkv, D]
         vseq = torch.from_numpy(gather_sequence(v_pool, v_scale, block_table[b], nk))
-        qb = torch.from_numpy(np.asarray(q[b, :, :ql], dtype=np.float32)).view(Hkv, G * ql, D)
+        qb = torch.from_numpy(np.ascontiguousarray(q[b, :, :ql], dtype=np.float32)).view(Hkv, G * ql, D)
         s = torch.einsum("hmd,khd->hmk", qb, kseq) * sm  # [Hkv, G*ql, nk]
         s = s.view(Hkv, G, ql, nk)
         mask = torch.from_numpy(np.arange(nk)[None, :] < lim[:, None])  # [ql, nk]

@@ -290,10 +290,41 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
   return PA_OK;
 }
 
-int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, void* stream) {
+// 4-D TMA map over Q [num_seqs, num_q_heads, max_q_len, 128] (d contiguous):
+// box = 64 columns x 128 rows, 128-byte swizzle; rows past max_q_len read as zeros.
+bool make_q_map(CUtensorMap* m, const pa_attn_io_t* io, int D, int B) {
+  auto enc = encode_fn();
+  if (!enc || D != 128) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(io->max_q_len),
+                              static_cast<cuuint64_t>(io->num_q_heads), static_cast<cuuint64_t>(B)};
+  const long long st[3] = {io->q_stride_row, io->q_stride_head, io->q_stride_seq};
+  for (long long x : st)
+    if (x <= 0) return false;
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[0] * 2), static_cast<cuuint64_t>(st[1] * 2),
+                                 static_cast<cuuint64_t>(st[2] * 2)};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(io->q), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, const pa_attn_io_t* io, void* stream) {
   if (p.B == 0 || p.maxq == 0) return PA_OK;
   if (p.B > 65535) return fail(PA_ERR_UNSUPPORTED, "prefill kernel supports at most 65535 sequences per call");
-  cudaError_t e = pa::launch_prefill(p, kv_kind(kv->dtype), kv->head_dim, kv->dtype == PA_DTYPE_BF16,
+  const int kvk = kv_kind(kv->dtype);
+  if (pa::prefill_tc_supported(kvk, kv->head_dim, kv->block_size) && !std::getenv("PIE_B200_NO_TCGEN05") &&
+      al(io->o, 16) && row_al(io->o_stride_seq, 2, 16) && row_al(io->o_stride_head, 2, 16) &&
+      row_al(io->o_stride_row, 2, 16)) {
+    pa::KvMaps maps;
+    CUtensorMap qmap;
+    if (make_kv_maps(kv, &maps) && make_q_map(&qmap, io, kv->head_dim, p.B)) {
+      cudaError_t e = pa::launch_prefill_tc(p, maps.k, maps.v, qmap, kvk, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "prefill (tcgen05) launch");
+      return PA_OK;
+    }
+  }
+  cudaError_t e = pa::launch_prefill(p, kvk, kv->head_dim, kv->dtype == PA_DTYPE_BF16,
                                      static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "prefill launch");
   return PA_OK;
@@ -421,7 +452,7 @@ int paged_attn_forward(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
   if (use_decode(p)) return run_decode(p, kv, workspace, workspace_bytes, stream);
-  return run_prefill(p, kv, stream);
+  return run_prefill(p, kv, io, stream);
 }
 
 int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
@@ -439,7 +470,7 @@ int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa
   pa::AttnParams p;
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
-  return run_prefill(p, kv, stream);
+  return run_prefill(p, kv, io, stream);
 }
 
 int kv_write_quant(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,

@@ -68,6 +68,7 @@ struct AttnParams {
   float sm_scale;
   int top_left;
   int* status;
+  unsigned int abort_gen;  // launch generation used by bounded waits to stop together
 };
 
 struct WriteParams {
@@ -109,5 +110,9 @@ int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, Deco
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
                           const DecodeLaunch& plan, cudaStream_t stream);
 cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);
+// tcgen05/TMEM prefill (16-bit pools, head_dim 128, block_size >= 8).
+bool prefill_tc_supported(int kv_kind, int D, int BS);
+cudaError_t launch_prefill_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                              const CUtensorMap& qmap, int kv_kind, cudaStream_t stream);
 
 }  // namespace pa

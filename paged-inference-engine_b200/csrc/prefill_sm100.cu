@@ -1,0 +1,387 @@
+// Causal paged prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces the q_len > 1 use of flash_attention_kernel
+// (kernels/flash_attention.py:19-136) for 16-bit pools with head_dim 128.
+// One CTA computes 128 query rows of one query head (FlashAttention-2
+// recurrence, kernels/flash_attention.py:102-123), with warp-specialised roles:
+//
+//   warp 4      TMA producer: the Q tile once, then K and V tiles of 128 keys
+//               gathered through the block table (one 4-D TMA box per block and
+//               per 64 columns of head_dim) into a two-stage ring.  Boxes past
+//               the sequence or of an out-of-pool block id are fetched at an
+//               out-of-range block coordinate, which TMA fills with zeros.
+//   warp 5      MMA issuer (one lane): S_j = Q K_j^T into one of two TMEM
+//               buffers (M=128, N=128, K=128 as 8 x K16 steps, both operands
+//               K-major SW128 in shared memory), then O += P_{j-1} V_{j-1} with
+//               P read from TMEM and V as an MN-major SW128 operand.
+//               tcgen05.commit signals S ready, the K/V stage free, and O done.
+//   warps 0..3  softmax: thread t owns query row t = TMEM lane t.  It reads its
+//               row of S, masks (bottom-right causal, sequence end), keeps the
+//               running max in base 2, writes P (fp16/bf16) over the S buffer,
+//               and rescales its O row in TMEM only when the max grows by more
+//               than 2^8 (the max is a stabiliser; a stale one leaves the
+//               result exact).  The epilogue normalises O and writes O and LSE.
+//
+// TMEM: S0 columns [0,128), S1 [128,256), O [256,384) of a 512-column
+// allocation; one CTA per SM (160 KB of shared memory).
+#include <atomic>
+
+#include "pa_common.cuh"
+
+namespace pa {
+namespace {
+
+constexpr int TC_BM = 128;        // query rows per CTA
+constexpr int TC_BN = 128;        // keys per tile
+constexpr int TC_D = 128;         // head_dim
+constexpr int TC_THREADS = 192;   // 4 softmax warps + producer + MMA
+constexpr int HALF_B = TC_BM * 128;               // one 64-column half of a 128-row tile: 16 KB
+constexpr int TILE_B = 2 * HALF_B;                // 32 KB
+constexpr int SQ_OFF = 0;
+constexpr int SK_OFF = TILE_B;                    // + stage * 2 * TILE_B
+constexpr int SV_OFF = 2 * TILE_B;
+constexpr int BAR_OFF = 5 * TILE_B;               // after Q + 2 stages of K and V
+constexpr int TC_SMEM = BAR_OFF + 256 + 1024;     // barriers + TMEM slot + alignment slack
+constexpr uint32_t TMEM_COLS = 512;
+__device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
+constexpr uint32_t O_COL = 256;
+constexpr float RESCALE_THRESHOLD = 8.0f;         // log2 units
+
+// barrier slots (8 bytes each) after BAR_OFF
+enum : int { B_QFULL = 0, B_QREADY = 1, B_KVFULL = 2, B_KVEMPTY = 4, B_SFULL = 6, B_PFULL = 8, B_ODONE = 10,
+             B_TMEMSLOT = 12 };
+
+struct alignas(64) TcMaps {
+  CUtensorMap k;
+  CUtensorMap v;
+  CUtensorMap q;
+};
+
+__device__ __forceinline__ int tc_seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
+
+__device__ __forceinline__ int tc_seq_keys(const AttnParams& p, int b, int q) {
+  if (q <= 0) return 0;
+  int nb = p.nblk[b];
+  if (nb > p.bt_cols) nb = p.bt_cols;
+  if (nb < 0) nb = 0;
+  long long nk = p.kvlen[b];
+  const long long cap = static_cast<long long>(nb) << p.log2BS;
+  if (nk > cap) nk = cap;
+  if (nk < 0) nk = 0;
+  if (p.top_left && nk > q) nk = q;
+  return static_cast<int>(nk);
+}
+
+// Launch generation of the last launch in which a wait gave up: once one CTA
+// times out, every other wait of that launch stops within ~1k polls instead of
+// running into its own limit.
+__device__ unsigned int g_tc_abort_gen = 0;
+
+// Bounded mbarrier wait; false (and a status bit) on time-out or abort.
+__device__ __noinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uint32_t parity) {
+  constexpr int kLimit = 1 << 20;
+  for (int i = 0; i < kLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *reinterpret_cast<volatile unsigned int*>(&g_tc_abort_gen) == p.abort_gen) return false;
+  }
+  atomicExch(&g_tc_abort_gen, p.abort_gen);
+  set_status(p.status, ST_WAIT_TIMEOUT);
+  return false;
+}
+
+template <bool MMA_BF16, bool Q_CONVERT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    pa_prefill_tc_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int mtile = gridDim.x - 1 - blockIdx.x;  // longest (causal) tiles first
+  const int hq = blockIdx.y;
+  const int b = blockIdx.z;
+  const int qlen = tc_seq_qlen(p, b);
+  const int m0 = mtile * TC_BM;
+  if (m0 >= qlen) return;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* sm = smem_raw + (base - raw);
+  const uint32_t bars = base + BAR_OFF;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  const int kvh = hq / p.G;
+  const int nkeys = tc_seq_keys(p, b, qlen);
+  const int off = p.top_left ? 0 : p.kvlen[b] - qlen;
+  const int kend = min(nkeys, off + m0 + TC_BM);
+  const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
+
+  if (tid == 0) {
+    mbar_init(bar(B_QFULL), 1);
+    mbar_init(bar(B_QREADY), 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(B_KVFULL + s), 1);
+      mbar_init(bar(B_KVEMPTY + s), 1);
+      mbar_init(bar(B_SFULL + s), 1);
+      mbar_init(bar(B_PFULL + s), 128);
+    }
+    mbar_init(bar(B_ODONE), 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(bar(B_TMEMSLOT), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + BAR_OFF + 8 * B_TMEMSLOT);
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nt > 0) {
+      mbar_arrive_expect_tx(bar(B_QFULL), TILE_B);
+      tma_load_4d(base + SQ_OFF, &maps.q, bar(B_QFULL), 0, m0, hq, b);
+      tma_load_4d(base + SQ_OFF + HALF_B, &maps.q, bar(B_QFULL), 64, m0, hq, b);
+      const int boxs = p.BS < 16 ? p.BS : 16;
+      const int nbox = TC_BN / boxs;
+      const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        if (j >= 2) wait_or_flag(p, bar(B_KVEMPTY + s), ((j >> 1) - 1) & 1);
+        mbar_arrive_expect_tx(bar(B_KVFULL + s), 2 * TILE_B);
+        const uint32_t kdst = base + SK_OFF + s * 2 * TILE_B;
+        const uint32_t vdst = base + SV_OFF + s * 2 * TILE_B;
+        for (int i = 0; i < nbox; ++i) {
+          const int key = j * TC_BN + i * boxs;
+          int blk = p.NB;  // out of range: TMA fills the box with zeros
+          int slot = 0;
+          if (key < nkeys) {
+            const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+            if (x >= 0 && x < p.NB) {
+              blk = x;
+              slot = key & (p.BS - 1);
+            } else {
+              set_status(p.status, ST_BAD_BLOCK_ID);
+            }
+          }
+          const uint32_t roff = static_cast<uint32_t>(i * boxs * 128);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tma_load_4d(kdst + h * HALF_B + roff, &maps.k, bar(B_KVFULL + s), 64 * h, kvh, slot, blk);
+            tma_load_4d(vdst + h * HALF_B + roff, &maps.v, bar(B_KVFULL + s), 64 * h, kvh, slot, blk);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t IDESC_QK = instr_desc_f16(MMA_BF16, false, false, TC_BM, TC_BN);
+      constexpr uint32_t IDESC_PV = instr_desc_f16(MMA_BF16, false, true, TC_BM, TC_D);
+      auto issue_pv = [&](int jj) {
+        const int s = jj & 1;
+        wait_or_flag(p, bar(B_PFULL + s), (jj >> 1) & 1);
+        tc_fence_after();
+        const uint32_t vbase = base + SV_OFF + s * 2 * TILE_B;
+#pragma unroll
+        for (int k = 0; k < TC_BN / 16; ++k) {
+          // V: MN-major SW128; LBO = distance between the two 64-column halves, SBO = 8 rows
+          const uint64_t bdesc = smem_desc(vbase + k * 16 * 128, HALF_B, 1024);
+          tc_mma_ts(tmem + O_COL, tmem + s_col(s) + 8 * k, bdesc, IDESC_PV, (jj > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(bar(B_KVEMPTY + s));
+        tc_commit(bar(B_ODONE));
+      };
+      wait_or_flag(p, bar(B_QREADY), 0);
+      tc_fence_after();
+      for (int j = 0; j < nt; ++j) {
+        const int s = j & 1;
+        wait_or_flag(p, bar(B_KVFULL + s), (j >> 1) & 1);
+        tc_fence_after();
+        const uint32_t kbase = base + SK_OFF + s * 2 * TILE_B;
+#pragma unroll
+        for (int k = 0; k < TC_D / 16; ++k) {
+          // K-major SW128: a K16 step advances 32 bytes inside the 128-byte row
+          const uint32_t koff = (k >> 2) * HALF_B + (k & 3) * 32;
+          tc_mma_ss(tmem + s_col(s), smem_desc(base + SQ_OFF + koff, 16, 1024), smem_desc(kbase + koff, 16, 1024),
+                    IDESC_QK, k > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(B_SFULL + s));
+        if (j > 0) issue_pv(j - 1);
+      }
+      issue_pv(nt - 1);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0..3)
+    const int row = m0 + tid;
+    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (nt > 0) {
+      wait_or_flag(p, bar(B_QFULL), 0);
+      if constexpr (Q_CONVERT) {
+        // Q arrives in its own 16-bit type; convert in place to the pool's type
+        uint4* q4 = reinterpret_cast<uint4*>(sm + SQ_OFF);
+#pragma unroll 4
+        for (int i = tid; i < TILE_B / 16; i += 128) {
+          uint4 v = q4[i];
+          v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
+          v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
+          v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
+          v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
+          q4[i] = v;
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar(B_QREADY));
+    }
+    const int lim = min(nkeys, off + row + 1);
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    for (int j = 0; j < nt; ++j) {
+      const int s = j & 1;
+      wait_or_flag(p, bar(B_SFULL + s), (j >> 1) & 1);
+      tc_fence_after();
+      float x[TC_BN];
+#pragma unroll
+      for (int c = 0; c < TC_BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + s_col(s) + 32 * c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[32 * c + i] = __uint_as_float(r[i]);
+      }
+      const int k0 = j * TC_BN;
+      const bool need_mask = (k0 + TC_BN > off + m0 + 1) || (k0 + TC_BN > nkeys);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < TC_BN; ++i) {
+        float v = x[i] * p.scale_log2;
+        if (need_mask && k0 + i >= lim) v = -INFINITY;
+        x[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      float alpha = 1.f;
+      bool resc = false;
+      if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
+        alpha = ex2(m_ref - mx);
+        resc = l > 0.f;
+        m_ref = mx;
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+        // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this row
+        wait_or_flag(p, bar(B_ODONE), (j - 1) & 1);
+        tc_fence_after();
+        const float a = resc ? alpha : 1.f;
+#pragma unroll
+        for (int c = 0; c < TC_D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + O_COL + 32 * c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * a);
+          tmem_st32(trow + O_COL + 32 * c, r);
+        }
+        tmem_wait_st();
+      }
+      l *= alpha;
+      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2(x[64 * c + 2 * i] - m_use);
+          const float p1 = ex2(x[64 * c + 2 * i + 1] - m_use);
+          l += p0 + p1;
+          pk[i] = pack2<MMA_BF16>(p0, p1);
+        }
+        tmem_st32(trow + s_col(s) + 32 * c, pk);
+      }
+      tmem_wait_st();
+      if (nkeys - k0 < TC_BN) {
+        // keys past the sequence: zero their V rows so that P = 0 contributes
+        // exactly nothing even if the pool slots hold non-finite bytes
+        if (k0 + tid >= nkeys) {
+          unsigned char* vrow = sm + SV_OFF + s * 2 * TILE_B + tid * 128;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + h * HALF_B + 16 * c) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(bar(B_PFULL + s));
+    }
+    // ---- epilogue: O / l, LSE ---------------------------------------------
+    const bool valid = row < qlen;
+    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
+    if (nt > 0) {
+      wait_or_flag(p, bar(B_ODONE), (nt - 1) & 1);
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < TC_D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + O_COL + 32 * c, r);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_f16(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+            w.y = pack_f16(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+            w.z = pack_f16(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+            w.w = pack_f16(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
+          }
+        }
+      }
+    } else if (valid) {
+      for (int d = 0; d < TC_D; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+    }
+    if (valid && p.lse) {
+      const float L = l > 0.f ? (m_ref + lg2(l)) * 0.6931471805599453f : -INFINITY;
+      static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+          __float2half_rn(L);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+bool prefill_tc_supported(int kv_kind, int D, int BS) {
+  return (kv_kind == KV_F16 || kv_kind == KV_BF16) && D == TC_D && BS >= 8;
+}
+
+cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                              const CUtensorMap& qmap, int kv_kind, cudaStream_t stream) {
+  if (p_in.B == 0 || p_in.maxq == 0) return cudaSuccess;
+  static std::atomic<unsigned int> generation{0};
+  AttnParams p = p_in;
+  p.abort_gen = ++generation;
+  if (p.abort_gen == 0) p.abort_gen = ++generation;
+  TcMaps maps;
+  maps.k = kmap;
+  maps.v = vmap;
+  maps.q = qmap;
+  const bool mma_bf16 = kv_kind == KV_BF16;
+  const bool convert = (p.q_bf16 != 0) != mma_bf16;
+  const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);
+  auto launch = [&](auto kern) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, TC_THREADS, TC_SMEM, stream>>>(p, maps);
+    return cudaGetLastError();
+  };
+  if (mma_bf16) return convert ? launch(pa_prefill_tc_kernel<true, true>) : launch(pa_prefill_tc_kernel<true, false>);
+  return convert ? launch(pa_prefill_tc_kernel<false, true>) : launch(pa_prefill_tc_kernel<false, false>);
+}
+
+}  // namespace pa
