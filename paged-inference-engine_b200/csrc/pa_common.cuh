@@ -264,6 +264,54 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(bool bf16, bool a_mn_major
          ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ---------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100 f32x2 FMA-pipe instructions) and 2^x on the FMA pipe.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x for a pair of floats without the MUFU unit.  Range reduction: adding
+// 1.5*2^23 rounds x to the nearest integer n inside the float's mantissa
+// (f = x - n in [-1/2, 1/2]); 2^f is a cubic whose coefficients were fitted
+// here by iteratively re-weighted least squares on the relative error over
+// [-1/2, 1/2] (max relative error 7.6e-5, 13.7 bits -- more than the 11 bits
+// an fp16 probability keeps); 2^n is applied by adding n to the exponent
+// field.  Inputs below -125 are clamped there (result ~2^-125).
+__device__ __forceinline__ void exp2_fma_x2(float& a, float& b) {
+  const float kMagic = 12582912.0f;  // 1.5 * 2^23
+  a = fmaxf(a, -125.0f);
+  b = fmaxf(b, -125.0f);
+  const uint64_t x = f2_pack(a, b);
+  const uint64_t t = f2_add(x, f2_pack(kMagic, kMagic));
+  const uint64_t n = f2_add(t, f2_pack(-kMagic, -kMagic));
+  const uint64_t f = f2_fma(n, f2_pack(-1.0f, -1.0f), x);
+  uint64_t poly = f2_fma(f2_pack(0.055170249193906784f, 0.055170249193906784f), f,
+                         f2_pack(0.24260790646076202f, 0.24260790646076202f));
+  poly = f2_fma(poly, f, f2_pack(0.693260908126831f, 0.693260908126831f));
+  poly = f2_fma(poly, f, f2_pack(0.9999282956123352f, 0.9999282956123352f));
+  float p0, p1, t0, t1;
+  f2_unpack(poly, p0, p1);
+  f2_unpack(t, t0, t1);
+  a = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  b = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ float load_scale(const void* base, long long off, int is_f32) {
   return is_f32 ? static_cast<const float*>(base)[off]
                 : __half2float(static_cast<const __half*>(base)[off]);

@@ -25,6 +25,7 @@
 // TMEM: S0 columns [0,128), S1 [128,256), O [256,384) of a 512-column
 // allocation; one CTA per SM (160 KB of shared memory).
 #include <atomic>
+#include <cstdlib>
 
 #include "pa_common.cuh"
 
@@ -46,6 +47,13 @@ constexpr uint32_t TMEM_COLS = 512;
 __device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
 constexpr uint32_t O_COL = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;         // log2 units
+// Pairs of probabilities whose index i satisfies (i & MASK) == MASK compute
+// 2^x with the FMA-pipe polynomial instead of MUFU.EX2 (MUFU throughput per SM
+// matches the tensor core's rate per score element for head_dim 128).
+#ifndef PA_EMU_EVERY_MASK
+#define PA_EMU_EVERY_MASK 3
+#endif
+constexpr int EMU_EVERY_MASK = PA_EMU_EVERY_MASK;
 
 // barrier slots (8 bytes each) after BAR_OFF
 enum : int { B_QFULL = 0, B_QREADY = 1, B_KVFULL = 2, B_KVEMPTY = 4, B_SFULL = 6, B_PFULL = 8, B_ODONE = 10,
@@ -354,6 +362,360 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Paired-head variant (grouped-query attention with an even group): one CTA
+// computes the same 128 query rows for two query heads of one KV group, so each
+// K/V tile is fetched once for both.  Two softmax warpgroups (warps 0-3: head a,
+// 4-7: head b) alternate with the tensor core: while one warpgroup turns S into
+// P, the MMA warp runs the other head's P*V and next Q*K^T ("ping-pong").
+// K and V have separate rings (3 and 2 stages) so a K stage is recycled as soon
+// as both Q*K^T products have consumed it.  TMEM: S_a [0,128), S_b [128,256),
+// O_a [256,384), O_b [384,512).
+// ---------------------------------------------------------------------------
+constexpr int P2_THREADS = 320;   // 2 softmax warpgroups + producer + MMA
+constexpr int P2_KS = 3;          // K stages
+constexpr int P2_VS = 2;          // V stages
+constexpr int P2_QA = 0;
+constexpr int P2_QB = TILE_B;
+constexpr int P2_K = 2 * TILE_B;
+constexpr int P2_V = P2_K + P2_KS * TILE_B;
+constexpr int P2_BAR = P2_V + P2_VS * TILE_B;     // 224 KB
+constexpr int P2_SMEM = P2_BAR + 256 + 1024;
+enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, C_VEMPTY = 10, C_SFULL = 12,
+             C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18 };
+
+template <bool MMA_BF16, bool Q_CONVERT>
+__global__ void __launch_bounds__(P2_THREADS, 1)
+    pa_prefill_tc2_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int mtile = gridDim.x - 1 - blockIdx.x;
+  const int pairs = p.G >> 1;
+  const int kvh = blockIdx.y / pairs;
+  const int hq0 = kvh * p.G + 2 * (blockIdx.y - kvh * pairs);
+  const int b = blockIdx.z;
+  const int qlen = tc_seq_qlen(p, b);
+  const int m0 = mtile * TC_BM;
+  if (m0 >= qlen) return;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* sm = smem_raw + (base - raw);
+  const uint32_t bars = base + P2_BAR;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  const int nkeys = tc_seq_keys(p, b, qlen);
+  const int off = p.top_left ? 0 : p.kvlen[b] - qlen;
+  const int kend = min(nkeys, off + m0 + TC_BM);
+  const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
+
+  if (tid == 0) {
+    mbar_init(bar(C_QFULL), 1);
+    mbar_init(bar(C_QREADY), 256);
+    for (int s = 0; s < P2_KS; ++s) {
+      mbar_init(bar(C_KFULL + s), 1);
+      mbar_init(bar(C_KEMPTY + s), 1);
+    }
+    for (int s = 0; s < P2_VS; ++s) {
+      mbar_init(bar(C_VFULL + s), 1);
+      mbar_init(bar(C_VEMPTY + s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar(C_SFULL + x), 1);
+      mbar_init(bar(C_PFULL + x), 128);
+      mbar_init(bar(C_ODONE + x), 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(bar(C_TMEMSLOT), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + P2_BAR + 8 * C_TMEMSLOT);
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nt > 0) {
+      mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, m0, hq0 + x, b);
+        tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, m0, hq0 + x, b);
+      }
+    }
+    if (nt > 0) {
+      // Lane i owns box i of every tile: the block ids of a tile are fetched in
+      // one round trip (and one tile ahead), and each lane issues its own boxes.
+      const int boxs = p.BS < 16 ? p.BS : 16;
+      const int nbox = TC_BN / boxs;  // <= 16 (block_size >= 8)
+      const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
+      auto fetch = [&](int j) {
+        const int key = j * TC_BN + lane * boxs;
+        int blk = p.NB;  // out of range: TMA fills the box with zeros
+        if (lane < nbox && key < nkeys) {
+          const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+          if (x >= 0 && x < p.NB) blk = x;
+          else set_status(p.status, ST_BAD_BLOCK_ID);
+        }
+        return blk;
+      };
+      int blk = fetch(0);
+      for (int j = 0; j < nt; ++j) {
+        const int blk_next = (j + 1 < nt) ? fetch(j + 1) : p.NB;
+        const int slot = (j * TC_BN + lane * boxs) & (p.BS - 1);
+        const uint32_t roff = static_cast<uint32_t>(lane * boxs * 128);
+        const int ks = j % P2_KS;
+        const int vs = j % P2_VS;
+        if (lane == 0) {
+          if (j >= P2_KS) wait_or_flag(p, bar(C_KEMPTY + ks), ((j / P2_KS) - 1) & 1);
+          mbar_arrive_expect_tx(bar(C_KFULL + ks), TILE_B);
+        }
+        __syncwarp();
+        if (lane < nbox) {
+          const uint32_t dst = base + P2_K + ks * TILE_B + roff;
+          tma_load_4d(dst, &maps.k, bar(C_KFULL + ks), 0, kvh, blk < p.NB ? slot : 0, blk);
+          tma_load_4d(dst + HALF_B, &maps.k, bar(C_KFULL + ks), 64, kvh, blk < p.NB ? slot : 0, blk);
+        }
+        if (lane == 0) {
+          if (j >= P2_VS) wait_or_flag(p, bar(C_VEMPTY + vs), ((j / P2_VS) - 1) & 1);
+          mbar_arrive_expect_tx(bar(C_VFULL + vs), TILE_B);
+        }
+        __syncwarp();
+        if (lane < nbox) {
+          const uint32_t dst = base + P2_V + vs * TILE_B + roff;
+          tma_load_4d(dst, &maps.v, bar(C_VFULL + vs), 0, kvh, blk < p.NB ? slot : 0, blk);
+          tma_load_4d(dst + HALF_B, &maps.v, bar(C_VFULL + vs), 64, kvh, blk < p.NB ? slot : 0, blk);
+        }
+        blk = blk_next;
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nt > 0) {
+      constexpr uint32_t IDESC_QK = instr_desc_f16(MMA_BF16, false, false, TC_BM, TC_BN);
+      constexpr uint32_t IDESC_PV = instr_desc_f16(MMA_BF16, false, true, TC_BM, TC_D);
+      auto qk = [&](int x, int j) {
+        const uint32_t kb = base + P2_K + (j % P2_KS) * TILE_B;
+        const uint32_t qb = base + (x ? P2_QB : P2_QA);
+#pragma unroll
+        for (int k = 0; k < TC_D / 16; ++k) {
+          const uint32_t koff = (k >> 2) * HALF_B + (k & 3) * 32;
+          tc_mma_ss(tmem + s_col(x), smem_desc(qb + koff, 16, 1024), smem_desc(kb + koff, 16, 1024), IDESC_QK,
+                    k > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(C_SFULL + x));
+      };
+      auto pv = [&](int x, int j) {
+        wait_or_flag(p, bar(C_PFULL + x), j & 1);
+        tc_fence_after();
+        const uint32_t vb = base + P2_V + (j % P2_VS) * TILE_B;
+#pragma unroll
+        for (int k = 0; k < TC_BN / 16; ++k)
+          tc_mma_ts(tmem + O_COL + 128 * x, tmem + s_col(x) + 8 * k, smem_desc(vb + k * 16 * 128, HALF_B, 1024),
+                    IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+        tc_commit(bar(C_ODONE + x));
+      };
+      wait_or_flag(p, bar(C_QREADY), 0);
+      wait_or_flag(p, bar(C_KFULL), 0);
+      tc_fence_after();
+      qk(0, 0);
+      qk(1, 0);
+      tc_commit(bar(C_KEMPTY));
+      for (int j = 0; j < nt; ++j) {
+        wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
+        pv(0, j);
+        const bool more = j + 1 < nt;
+        if (more) {
+          wait_or_flag(p, bar(C_KFULL + (j + 1) % P2_KS), ((j + 1) / P2_KS) & 1);
+          tc_fence_after();
+          qk(0, j + 1);
+        }
+        pv(1, j);
+        tc_commit(bar(C_VEMPTY + j % P2_VS));
+        if (more) {
+          qk(1, j + 1);
+          tc_commit(bar(C_KEMPTY + (j + 1) % P2_KS));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0-7)
+    const int x = warp >> 2;     // 0: head a, 1: head b
+    const int r = tid & 127;     // query row within the tile = TMEM lane
+    const int row = m0 + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t scol = s_col(x);
+    const uint32_t ocol = O_COL + 128 * x;
+    if (nt > 0) {
+      wait_or_flag(p, bar(C_QFULL), 0);
+      if constexpr (Q_CONVERT) {
+        uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
+#pragma unroll 4
+        for (int i = r; i < TILE_B / 16; i += 128) {
+          uint4 v = q4[i];
+          v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
+          v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
+          v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
+          v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
+          q4[i] = v;
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar(C_QREADY));
+    }
+    const int lim = min(nkeys, off + row + 1);
+    float m_ref = -INFINITY;
+    float l = 0.f;
+    for (int j = 0; j < nt; ++j) {
+      wait_or_flag(p, bar(C_SFULL + x), j & 1);
+      tc_fence_after();
+      const int k0 = j * TC_BN;
+      const bool need_mask = (k0 + TC_BN > off + m0 + 1) || (k0 + TC_BN > nkeys);
+      // pass 1: row max of the raw logits (the scale is positive), masked on
+      // diagonal / sequence-end tiles; two TMEM loads in flight per wait
+      float mraw = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < TC_BN / 64; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(trow + scol + 64 * c, r0);
+        tmem_ld32(trow + scol + 64 * c + 32, r1);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (k0 + 64 * c + i < lim) mraw = fmaxf(mraw, __uint_as_float(r0[i]));
+            if (k0 + 64 * c + 32 + i < lim) mraw = fmaxf(mraw, __uint_as_float(r1[i]));
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
+        }
+      }
+      const float mx = mraw * p.scale_log2;
+      float alpha = 1.f;
+      bool resc = false;
+      if (mx > m_ref + RESCALE_THRESHOLD) {
+        alpha = ex2(m_ref - mx);
+        resc = l > 0.f;
+        m_ref = mx;
+      }
+      if (__any_sync(0xffffffffu, resc)) {
+        wait_or_flag(p, bar(C_ODONE + x), (j - 1) & 1);
+        tc_fence_after();
+        const float a = resc ? alpha : 1.f;
+#pragma unroll
+        for (int c = 0; c < TC_D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(trow + ocol + 32 * c, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
+          tmem_st32(trow + ocol + 32 * c, rr);
+        }
+        tmem_wait_st();
+      }
+      l *= alpha;
+      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      const float c2 = p.scale_log2;
+      // pass 2: P = 2^(s*c - m) packed in pairs over the S columns already read
+      float lsum[2] = {0.f, 0.f};  // two independent accumulation chains
+#pragma unroll
+      for (int c = 0; c < TC_BN / 64; ++c) {
+        uint32_t r0[32], r1[32], pk[32];
+        tmem_ld32(trow + scol + 64 * c, r0);
+        tmem_ld32(trow + scol + 64 * c + 32, r1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t* rr = h ? r1 : r0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float p0, p1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                             f2_pack(neg_m, neg_m)),
+                      p0, p1);
+            if ((i & EMU_EVERY_MASK) == EMU_EVERY_MASK) {
+              exp2_fma_x2(p0, p1);  // this share of the exponentials runs on the FMA pipe
+            } else {
+              p0 = ex2(p0);
+              p1 = ex2(p1);
+            }
+            if (need_mask) {
+              const int kk = k0 + 64 * c + 32 * h + 2 * i;
+              if (kk >= lim) p0 = 0.f;
+              if (kk + 1 >= lim) p1 = 0.f;
+            }
+            lsum[h] += p0 + p1;
+            pk[16 * h + i] = pack2<MMA_BF16>(p0, p1);
+          }
+        }
+        tmem_st32(trow + scol + 32 * c, pk);
+      }
+      l += lsum[0] + lsum[1];
+      tmem_wait_st();
+      if (x == 0 && nkeys - k0 < TC_BN) {
+        // keys past the sequence: zero their V rows (head a's P*V runs first)
+        wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
+        if (k0 + r >= nkeys) {
+          unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + r * 128;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + h * HALF_B + 16 * c) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(bar(C_PFULL + x));
+    }
+    // ---- epilogue ------------------------------------------------------------
+    const int hq = hq0 + x;
+    const bool valid = row < qlen;
+    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
+    if (nt > 0) {
+      wait_or_flag(p, bar(C_ODONE + x), (nt - 1) & 1);
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < TC_D / 32; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(trow + ocol + 32 * c, rr);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+            w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+            w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+            w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
+          }
+        }
+      }
+    } else if (valid) {
+      for (int d = 0; d < TC_D; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+    }
+    if (valid && p.lse) {
+      const float L = l > 0.f ? (m_ref + lg2(l)) * 0.6931471805599453f : -INFINITY;
+      static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+          __float2half_rn(L);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 bool prefill_tc_supported(int kv_kind, int D, int BS) {
@@ -373,6 +735,17 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
   maps.q = qmap;
   const bool mma_bf16 = kv_kind == KV_BF16;
   const bool convert = (p.q_bf16 != 0) != mma_bf16;
+  if ((p.G & 1) == 0 && !std::getenv("PIE_B200_TC_SINGLE")) {
+    const dim3 grid2((p.maxq + TC_BM - 1) / TC_BM, p.Hkv * (p.G / 2), p.B);
+    auto launch2 = [&](auto kern) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM);
+      if (e != cudaSuccess) return e;
+      kern<<<grid2, P2_THREADS, P2_SMEM, stream>>>(p, maps);
+      return cudaGetLastError();
+    };
+    if (mma_bf16) return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
+    return convert ? launch2(pa_prefill_tc2_kernel<false, true>) : launch2(pa_prefill_tc2_kernel<false, false>);
+  }
   const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);
   auto launch = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
