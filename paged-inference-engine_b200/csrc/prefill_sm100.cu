@@ -244,6 +244,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int lim = min(nkeys, off + row + 1);
     float m_ref = -INFINITY;
     float l = 0.f;
+    // O-done phases are consumed one by one and never more than one phase
+    // away from the barrier: a parity wait on a phase two ahead succeeds at
+    // once, one on a phase two behind never does.
+    int od = 0;
+    auto wait_o_done = [&](int k) {
+      for (; od <= k; ++od) wait_or_flag(p, bar(B_ODONE), od & 1);
+    };
     for (int j = 0; j < nt; ++j) {
       const int s = j & 1;
       wait_or_flag(p, bar(B_SFULL + s), (j >> 1) & 1);
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if (__any_sync(0xffffffffu, resc)) {
         // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this row
-        wait_or_flag(p, bar(B_ODONE), (j - 1) & 1);
+        wait_o_done(j - 1);
         tc_fence_after();
         const float a = resc ? alpha : 1.f;
 #pragma unroll
@@ -317,6 +324,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         fence_proxy_async_smem();
       }
+      // stay within one phase of the O-done barrier (P*V(j-1) finished long ago)
+      if (j >= 1) wait_o_done(j - 1);
       tc_fence_before();
       mbar_arrive(bar(B_PFULL + s));
     }
@@ -324,7 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const bool valid = row < qlen;
     __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
     if (nt > 0) {
-      wait_or_flag(p, bar(B_ODONE), (nt - 1) & 1);
+      wait_o_done(nt - 1);
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
@@ -571,6 +580,13 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     const int lim = min(nkeys, off + row + 1);
     float m_ref = -INFINITY;
     float l = 0.f;
+    // O-done phases are consumed one by one and never more than one phase
+    // away from the barrier: a parity wait on a phase two ahead succeeds at
+    // once, one on a phase two behind never does.
+    int od = 0;
+    auto wait_o_done = [&](int k) {
+      for (; od <= k; ++od) wait_or_flag(p, bar(C_ODONE + x), od & 1);
+    };
     for (int j = 0; j < nt; ++j) {
       wait_or_flag(p, bar(C_SFULL + x), j & 1);
       tc_fence_after();
@@ -593,7 +609,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
+          for (int i = 0; i < 32; ++i) mraw = fmax3f(mraw, __uint_as_float(r0[i]), __uint_as_float(r1[i]));
         }
       }
       const float mx = mraw * p.scale_log2;
@@ -605,7 +621,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         m_ref = mx;
       }
       if (__any_sync(0xffffffffu, resc)) {
-        wait_or_flag(p, bar(C_ODONE + x), (j - 1) & 1);
+        wait_o_done(j - 1);
         tc_fence_after();
         const float a = resc ? alpha : 1.f;
 #pragma unroll
@@ -623,7 +639,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
       const float c2 = p.scale_log2;
       // pass 2: P = 2^(s*c - m) packed in pairs over the S columns already read
-      float lsum[2] = {0.f, 0.f};  // two independent accumulation chains
+      uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};  // packed pairs, two chains
 #pragma unroll
       for (int c = 0; c < TC_BN / 64; ++c) {
         uint32_t r0[32], r1[32], pk[32];
@@ -650,13 +666,18 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
               if (kk >= lim) p0 = 0.f;
               if (kk + 1 >= lim) p1 = 0.f;
             }
-            lsum[h] += p0 + p1;
+            lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
             pk[16 * h + i] = pack2<MMA_BF16>(p0, p1);
           }
         }
         tmem_st32(trow + scol + 32 * c, pk);
       }
-      l += lsum[0] + lsum[1];
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(lsum2[0], a0, a1);
+        f2_unpack(lsum2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
       tmem_wait_st();
       if (x == 0 && nkeys - k0 < TC_BN) {
         // keys past the sequence: zero their V rows (head a's P*V runs first)
@@ -670,6 +691,8 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         }
         fence_proxy_async_smem();
       }
+      // stay within one phase of the O-done barrier (P*V(j-1) finished long ago)
+      if (j >= 1) wait_o_done(j - 1);
       tc_fence_before();
       mbar_arrive(bar(C_PFULL + x));
     }
@@ -678,7 +701,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     const bool valid = row < qlen;
     __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
     if (nt > 0) {
-      wait_or_flag(p, bar(C_ODONE + x), (nt - 1) & 1);
+      wait_o_done(nt - 1);
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
