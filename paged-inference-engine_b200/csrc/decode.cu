@@ -7,7 +7,7 @@
 // idle, and reads every KV head once per query head.
 //
 // Design (B200, HBM-bound):
-//  * Work unit = a 16-key TILE of one (sequence, kv head) SEGMENT.  All tiles
+//  * Work unit = a TILE of 16 keys (32 for int8 pools) of one (sequence, kv head) SEGMENT.  All tiles
 //    of all segments form one flat list (segment-major); a persistent grid of
 //    W warps gives warp w the contiguous range [w*chunk, (w+1)*chunk) with
 //    chunk = ceil(total / W) ("stream-K"): every warp streams the same number
@@ -39,7 +39,6 @@
 namespace pa {
 namespace {
 
-constexpr int TILE = 16;
 constexpr int NC_MAX = 16;      // max packed columns (q rows x group heads)
 // Worker warps per CTA (upper bound): 12 for single-n-tile variants (<= 170
 // registers per thread), 8 for the two-n-tile ones.
@@ -55,21 +54,32 @@ constexpr int META_B = 16;      // per stage: [0] fp16 half-select mask of the s
 #define PA_DEC_STAGE_BUDGET_I8 (17 * 1024)
 #endif
 
+#ifndef PA_DEC_TILE_I8
+#define PA_DEC_TILE_I8 32
+#endif
+
 template <int D, int KVT>
 struct DecCfg {
   static constexpr bool INT8 = KVT == KV_I8;
   static constexpr int ELT = INT8 ? 1 : 2;
+  // Keys per tile: 16 for 16-bit pools (8 KB of K+V at D=128), 32 for int8
+  // pools, so an int8 tile carries as many bytes and twice the independent
+  // MMA / conversion chains per softmax step.
+  static constexpr int TK = INT8 ? PA_DEC_TILE_I8 : 16;
+  static constexpr int KST = TK / 16;                  // 16-key MMA steps per tile
+  static constexpr int MAXBOX = TK / 8;                // TMA boxes per tile (block_size >= 8)
   static constexpr int ROWB = D * ELT;                 // bytes of one key row of one head
   static constexpr int CHUNKS = ROWB / 16;
-  static constexpr int TILEB = TILE * ROWB;            // K (or V) tile bytes, multiple of 1024
+  static constexpr int TILEB = TK * ROWB;              // K (or V) tile bytes, multiple of 1024
   static constexpr int HALVES = ROWB >= 128 ? ROWB / 128 : 1;  // TMA boxes across head_dim
   static constexpr int BOXD = (ROWB >= 128 ? 128 : ROWB) / ELT;
-  static constexpr int SCB = (INT8 ? 128 : 0) + META_B;  // scale words + meta
+  static constexpr int SCB = (INT8 ? 8 * TK : 0) + META_B;  // K + V scale words, then meta
   static constexpr int STAGE_RAW = 2 * TILEB + SCB + 8;
   static constexpr int STAGES_RAW = (INT8 ? PA_DEC_STAGE_BUDGET_I8 : PA_DEC_STAGE_BUDGET) / STAGE_RAW;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int ROWS_PER_IT = 32 / CHUNKS;
-  static constexpr int LOAD_ITS = TILE / ROWS_PER_IT;
+  static constexpr int LOAD_ITS = TK / ROWS_PER_IT;
+  static_assert(TK == 16 || TK == 32, "tiles hold 16 or 32 keys");
   static_assert(TILEB % 1024 == 0, "tiles must keep TMA swizzle atoms aligned");
 };
 
@@ -82,7 +92,7 @@ struct DecLayout {
   static constexpr int SC_OFF = 2 * S * C::TILEB;
   static constexpr int BAR_OFF = SC_OFF + S * C::SCB;
   static constexpr int P_OFF = (BAR_OFF + S * 8 + 15) & ~15;  // ldmatrix rows need 16-byte alignment
-  static constexpr int PB = TILE * 8 * NT * 2;
+  static constexpr int PB = C::TK * 8 * NT * 2;
   static constexpr int WARPB = ((P_OFF + PB) + 1023) & ~1023;
   static_assert(V_OFF % 1024 == 0 && C::TILEB % 1024 == 0, "TMA boxes need 1024-byte aligned tiles");
   static_assert(SC_OFF % 16 == 0 && C::SCB % 16 == 0, "scale words / meta must stay 16-byte aligned");
@@ -90,16 +100,21 @@ struct DecLayout {
   static_assert(P_OFF % 16 == 0 && WARPB % 1024 == 0, "P buffer / warp regions alignment");
 };
 
-// Byte offset of 16-byte chunk `ch` of key row `row` inside a tile.  This is
-// the layout TMA writes with SWIZZLE_128B (128-byte rows, one 2 KB box per
-// 128 bytes of head_dim) or SWIZZLE_64B (64-byte rows); the cp.async loader
-// writes the same layout.  The XOR makes the ldmatrix / LDS fragment reads
-// bank-conflict free (2-way for INT8 K at D=128).
-template <int ROWB>
+// Byte offset of 16-byte chunk `ch` of key row `row` inside a tile of TK
+// rows.  This is the layout TMA writes with SWIZZLE_128B (128-byte rows, one
+// box column of TK x 128 bytes per 128 bytes of head_dim) or SWIZZLE_64B
+// (64-byte rows); the cp.async loader writes the same layout.  The XOR makes
+// the ldmatrix / LDS fragment reads bank-conflict free (2-way for INT8 K at
+// D=128).
+template <int ROWB, int TK>
 __device__ __forceinline__ int toff(int row, int ch) {
-  if constexpr (ROWB >= 128) return (ch >> 3) * (TILE * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
+  if constexpr (ROWB >= 128) return (ch >> 3) * (TK * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4);
   else return row * 64 + ((ch ^ ((row >> 1) & 3)) << 4);
 }
+
+// Row mask of a whole tile.
+template <int TK>
+__device__ __forceinline__ unsigned tile_rows() { return TK == 32 ? 0xffffffffu : ((1u << TK) - 1u); }
 
 // Query rows of sequence b, never more than the rows Q holds.
 __device__ __forceinline__ int seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
@@ -155,76 +170,88 @@ __device__ __forceinline__ void cursor_next(const AttnParams& p, const int* ts, 
   if (c.b < p.B) cursor_seq(p, ts, c);
 }
 
-// Scale words of one tile (INT8): lanes 0..15 fetch the K scale of rows
-// 0..15, lanes 16..31 the V scale, each as the aligned 4-byte word holding it;
-// the half-select bits go to the stage meta word 0.
-template <int D, int KVT>
-__device__ __forceinline__ void load_scales(const AttnParams& p, const Cursor& c, unsigned char* sc, int lane) {
-  const int row = lane & 15;
-  const int key = c.tile * TILE + row;
-  bool ok = key < c.nkeys;
-  int blk = 0, slot = 0;
-  if (ok) {
-    blk = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
-    slot = key & (p.BS - 1);
-    ok = blk >= 0 && blk < p.NB;
-  }
+// Scale words of one tile (INT8).  In pass h, lanes 0..15 fetch the K scale
+// of rows 16h..16h+15 and lanes 16..31 the V scale, each as the aligned 4-byte
+// word holding it; the fp16 half-select bits go to meta words 0 (K) and 2 (V).
+// rb[h] is the block id of this lane's row in pass h.
+template <int TK>
+__device__ __forceinline__ void load_scales(const AttnParams& p, const Cursor& c, unsigned char* sc, unsigned* meta,
+                                            int lane, const int (&rb)[TK / 16]) {
   const bool isv = lane >= 16;
-  unsigned long long addr = reinterpret_cast<unsigned long long>(isv ? p.vs : p.ks);
-  if (ok) {
-    const long long off = isv ? (blk * p.vs_sblk + slot * p.vs_sslot + c.kvh * p.vs_shead)
-                              : (blk * p.ks_sblk + slot * p.ks_sslot + c.kvh * p.ks_shead);
-    addr += static_cast<unsigned long long>(off) * (p.scale_f32 ? 4 : 2);
+  unsigned kmask = 0, vmask = 0;
+#pragma unroll
+  for (int h = 0; h < TK / 16; ++h) {
+    const int row = (lane & 15) + 16 * h;
+    const int key = c.tile * TK + row;
+    const int blk = rb[h];
+    const bool ok = key < c.nkeys && blk >= 0 && blk < p.NB;
+    const int slot = key & (p.BS - 1);
+    unsigned long long addr = reinterpret_cast<unsigned long long>(isv ? p.vs : p.ks);
+    if (ok) {
+      const long long off = isv ? (blk * p.vs_sblk + slot * p.vs_sslot + c.kvh * p.vs_shead)
+                                : (blk * p.ks_sblk + slot * p.ks_sslot + c.kvh * p.ks_shead);
+      addr += static_cast<unsigned long long>(off) * (p.scale_f32 ? 4 : 2);
+    }
+    const unsigned hi = (!p.scale_f32 && ((addr >> 1) & 1)) ? 1u : 0u;
+    const unsigned m = __ballot_sync(0xffffffffu, hi);
+    kmask |= (m & 0xffffu) << (16 * h);
+    vmask |= (m >> 16) << (16 * h);
+    cp_async_4(smem_u32(sc) + (isv ? 4 * TK : 0) + row * 4, reinterpret_cast<const void*>(addr & ~3ull), ok ? 4 : 0);
   }
-  const unsigned hi = (!p.scale_f32 && ((addr >> 1) & 1)) ? 1u : 0u;
-  const unsigned mask = __ballot_sync(0xffffffffu, hi);
-  cp_async_4(smem_u32(sc) + lane * 4, reinterpret_cast<const void*>(addr & ~3ull), ok ? 4 : 0);
-  if (lane == 0) reinterpret_cast<unsigned*>(sc + 128)[0] = mask;
+  if (lane == 0) {
+    meta[0] = kmask;
+    meta[2] = vmask;
+  }
 }
 
 // TMA fetch of one tile (lane 0): one box of min(16, block_size) slots per
-// block touched and per 128 bytes of head_dim, for K and for V.  Rows that
-// are not fetched (beyond the sequence, or of a block id outside the pool)
-// are recorded in the stage's "missing rows" mask.
+// block touched and per 128 bytes of head_dim, for K and for V.  bx[j] is
+// the block id of box j.  Rows that are not fetched (beyond the sequence, or
+// of a block id outside the pool) are recorded in the stage's "missing rows"
+// mask.
 template <int D, int KVT>
 __device__ __forceinline__ void issue_tile_tma(const AttnParams& p, const KvMaps& maps, const Cursor& c,
-                                               uint32_t kdst, uint32_t vdst, uint32_t bar, unsigned* meta) {
+                                               uint32_t kdst, uint32_t vdst, uint32_t bar, unsigned* meta,
+                                               const int (&bx)[DecCfg<D, KVT>::MAXBOX]) {
   using C = DecCfg<D, KVT>;
-  const int key0 = c.tile * TILE;
-  const int boxs = p.BS < TILE ? p.BS : TILE;  // 8 or 16 (TMA mode needs block_size >= 8)
-  const int nbox = TILE / boxs;
-  int blks[2] = {-1, -1};
-  int slots[2] = {0, 0};
+  constexpr int TK = C::TK;
+  constexpr int RB = C::ROWB >= 128 ? 128 : C::ROWB;
+  const int key0 = c.tile * TK;
+  const int boxs = p.BS < 16 ? p.BS : 16;  // 8 or 16 (TMA mode needs block_size >= 8)
+  const int nbox = TK / boxs;
   unsigned missing = 0;
+  unsigned fetch = 0;
   uint32_t bytes = 0;
-  for (int j = 0; j < nbox; ++j) {
+#pragma unroll
+  for (int j = 0; j < C::MAXBOX; ++j) {
+    if (j >= nbox) break;
     const int k = key0 + j * boxs;
     const unsigned rows = ((1u << boxs) - 1u) << (j * boxs);
     if (k >= c.nkeys) {
       missing |= rows;
       continue;
     }
-    const int blk = __ldg(c.bt_row + static_cast<long long>(k >> p.log2BS) * p.bt_sc);
-    if (blk < 0 || blk >= p.NB) {
+    if (bx[j] < 0 || bx[j] >= p.NB) {
       set_status(p.status, ST_BAD_BLOCK_ID);
       missing |= rows;
       continue;
     }
-    blks[j] = blk;
-    slots[j] = k & (p.BS - 1);
-    bytes += 2u * C::HALVES * boxs * (C::ROWB >= 128 ? 128 : C::ROWB);
+    fetch |= 1u << j;
+    bytes += 2u * C::HALVES * boxs * RB;
   }
   const int valid = c.nkeys - key0;
-  if (valid < TILE) missing |= 0xffffu & ~((1u << (valid > 0 ? valid : 0)) - 1u);
+  if (valid < TK) missing |= tile_rows<TK>() & ~(valid > 0 ? ((1u << valid) - 1u) : 0u);
   meta[1] = missing;
   mbar_arrive_expect_tx(bar, bytes);
-  for (int j = 0; j < nbox; ++j) {
-    if (blks[j] < 0) continue;
+#pragma unroll
+  for (int j = 0; j < C::MAXBOX; ++j) {
+    if (!((fetch >> j) & 1u)) continue;
+    const int slot = (key0 + j * boxs) & (p.BS - 1);
 #pragma unroll
     for (int h = 0; h < C::HALVES; ++h) {
-      const uint32_t off = h * (TILE * 128) + j * boxs * (C::ROWB >= 128 ? 128 : C::ROWB);
-      tma_load_4d(kdst + off, &maps.k, bar, h * C::BOXD, c.kvh, slots[j], blks[j]);
-      tma_load_4d(vdst + off, &maps.v, bar, h * C::BOXD, c.kvh, slots[j], blks[j]);
+      const uint32_t off = h * (TK * 128) + j * boxs * RB;
+      tma_load_4d(kdst + off, &maps.k, bar, h * C::BOXD, c.kvh, slot, bx[j]);
+      tma_load_4d(vdst + off, &maps.v, bar, h * C::BOXD, c.kvh, slot, bx[j]);
     }
   }
 }
@@ -235,7 +262,8 @@ template <int D, int KVT>
 __device__ __forceinline__ void issue_tile_cpasync(const AttnParams& p, const Cursor& c, uint32_t kdst,
                                                    uint32_t vdst, unsigned* meta, int lane) {
   using C = DecCfg<D, KVT>;
-  const int key0 = c.tile * TILE;
+  constexpr int TK = C::TK;
+  const int key0 = c.tile * TK;
   const char* kbase = static_cast<const char*>(p.k);
   const char* vbase = static_cast<const char*>(p.v);
   const int ch = lane % C::CHUNKS;
@@ -259,8 +287,8 @@ __device__ __forceinline__ void issue_tile_cpasync(const AttnParams& p, const Cu
       ksrc = kbase + (blk * p.k_sblk + slot * p.k_sslot + c.kvh * p.k_shead) * C::ELT + ch * 16;
       vsrc = vbase + (blk * p.v_sblk + slot * p.v_sslot + c.kvh * p.v_shead) * C::ELT + ch * 16;
     }
-    cp_async_16(kdst + toff<C::ROWB>(row, ch), ksrc, ok ? 16 : 0);
-    cp_async_16(vdst + toff<C::ROWB>(row, ch), vsrc, ok ? 16 : 0);
+    cp_async_16(kdst + toff<C::ROWB, TK>(row, ch), ksrc, ok ? 16 : 0);
+    cp_async_16(vdst + toff<C::ROWB, TK>(row, ch), vsrc, ok ? 16 : 0);
   }
   if (lane == 0) meta[1] = 0u;
 }
@@ -278,6 +306,8 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   using Lay = DecLayout<D, KVT, NT>;
   constexpr int STAGES = C::STAGES;
   constexpr bool INT8 = C::INT8;
+  constexpr int TK = C::TK;
+  constexpr int KST = C::KST;
   constexpr bool MMA_BF16 = (KVT == KV_BF16);
   constexpr bool QIS_BF16 = (QT == Q_BF16);
   constexpr bool USE_CPASYNC = !TMA || INT8;  // cp.async carries tiles (no TMA) or scale words (INT8)
@@ -301,7 +331,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   for (int i = tid; i < p.B; i += NW * 32) {
     const int nk = seq_keys(p, i);
     if (p.nblk[i] > p.bt_cols) set_status(p.status, ST_BAD_NUM_BLOCKS);
-    s_ts[i] = (nk + TILE - 1) / TILE;
+    s_ts[i] = (nk + TK - 1) / TK;
   }
   if constexpr (TMA) {
     if (lane == 0) {
@@ -346,23 +376,69 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   cursor_locate(p, s_ts, g0, ld);
   cp = ld;
 
-  auto issue = [&](int slot_idx) {
+  // ---- block-table window (TMA path) ---------------------------------------
+  // Lane l holds the block id of box (l mod nbox) of tile win_base + l / nbox
+  // of this warp's range; the next window is loaded one window ahead, so no
+  // dependent block-table read sits between a tile's issue and its compute.
+  const int lnb = (TK == 32 ? 1 : 0) + (p.BS < 16 ? 1 : 0);  // log2(boxes per tile)
+  const int lbs = p.BS < 16 ? 3 : 4;                           // log2(box rows)
+  const int wt = 32 >> lnb;                                    // tiles per window
+  auto fetch_window = [&](int t0) -> int {
+    const int g = g0 + t0 + (lane >> lnb);
+    int v = 0;
+    if (g < g1) {
+      Cursor c;
+      cursor_locate(p, s_ts, g, c);
+      const int key = c.tile * TK + ((lane & ((1 << lnb) - 1)) << lbs);
+      if (key < c.nkeys) v = __ldg(c.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+    }
+    return v;
+  };
+  int win_base = 0, win_cur = 0, win_nxt = 0;
+  if constexpr (TMA) {
+    win_cur = fetch_window(0);
+    win_nxt = fetch_window(wt);
+  }
+
+  auto issue = [&](int ti, int slot_idx) {
     const uint32_t kdst = wbase_u32 + Lay::K_OFF + slot_idx * C::TILEB;
     const uint32_t vdst = wbase_u32 + Lay::V_OFF + slot_idx * C::TILEB;
     unsigned char* sc = wsm + Lay::SC_OFF + slot_idx * C::SCB;
-    unsigned* meta = reinterpret_cast<unsigned*>(sc + (INT8 ? 128 : 0));
+    unsigned* meta = reinterpret_cast<unsigned*>(sc + (INT8 ? 8 * TK : 0));
+    int rb[KST];
     if constexpr (TMA) {
-      if (lane == 0) issue_tile_tma<D, KVT>(p, maps, ld, kdst, vdst, wbase_u32 + Lay::BAR_OFF + 8 * slot_idx, meta);
+      if (ti - win_base >= wt) {
+        win_cur = win_nxt;
+        win_base += wt;
+        win_nxt = fetch_window(win_base + wt);
+      }
+      const int sl = (ti - win_base) << lnb;
+      int bx[C::MAXBOX];
+#pragma unroll
+      for (int j = 0; j < C::MAXBOX; ++j) bx[j] = __shfl_sync(0xffffffffu, win_cur, (sl + j) & 31);
+      if (lane == 0) issue_tile_tma<D, KVT>(p, maps, ld, kdst, vdst, wbase_u32 + Lay::BAR_OFF + 8 * slot_idx, meta, bx);
+      if constexpr (INT8) {
+#pragma unroll
+        for (int h = 0; h < KST; ++h)
+          rb[h] = __shfl_sync(0xffffffffu, win_cur, (sl + (((lane & 15) + 16 * h) >> lbs)) & 31);
+      }
     } else {
       issue_tile_cpasync<D, KVT>(p, ld, kdst, vdst, meta, lane);
+      if constexpr (INT8) {
+#pragma unroll
+        for (int h = 0; h < KST; ++h) {
+          const int key = ld.tile * TK + (lane & 15) + 16 * h;
+          rb[h] = key < ld.nkeys ? __ldg(ld.bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc) : 0;
+        }
+      }
     }
-    if constexpr (INT8) load_scales<D, KVT>(p, ld, sc, lane);
+    if constexpr (INT8) load_scales<TK>(p, ld, sc, meta, lane, rb);
   };
 
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
     if (g0 + s < g1) {
-      issue(s);
+      issue(s, s);
       cursor_next(p, s_ts, ld);
     }
     if constexpr (USE_CPASYNC) cp_async_commit();
@@ -385,7 +461,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
     }
     __syncwarp();
     if (g + STAGES - 1 < g1) {
-      issue((i + STAGES - 1) % STAGES);
+      issue(i + STAGES - 1, (i + STAGES - 1) % STAGES);
       cursor_next(p, s_ts, ld);
     }
     if constexpr (USE_CPASYNC) cp_async_commit();
@@ -466,119 +542,132 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
     unsigned char* kt = wsm + Lay::K_OFF + slot_idx * C::TILEB;
     unsigned char* vt = wsm + Lay::V_OFF + slot_idx * C::TILEB;
     unsigned char* sc = wsm + Lay::SC_OFF + slot_idx * C::SCB;
+    const unsigned* meta = reinterpret_cast<const unsigned*>(sc + (INT8 ? 8 * TK : 0));
     const uint32_t sk = smem_u32(kt);
     const uint32_t sv = smem_u32(vt);
     zeroed_prev = false;
     if constexpr (TMA && !INT8) {
       // rows not fetched (or past the sequence) may hold stale or non-finite
       // bytes: zero them in V so that P = 0 really contributes nothing.
-      const unsigned missing = reinterpret_cast<const unsigned*>(sc)[1];
+      const unsigned missing = meta[1];
       if (missing) {
-        for (int idx = lane; idx < TILE * C::CHUNKS; idx += 32) {
+        for (int idx = lane; idx < TK * C::CHUNKS; idx += 32) {
           const int row = idx / C::CHUNKS;
           if ((missing >> row) & 1u)
-            *reinterpret_cast<uint4*>(vt + toff<C::ROWB>(row, idx % C::CHUNKS)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vt + toff<C::ROWB, TK>(row, idx % C::CHUNKS)) = make_uint4(0, 0, 0, 0);
         }
         zeroed_prev = true;
         __syncwarp();
       }
     }
 
-    // ---- S^T = K * Q^T -----------------------------------------------------
-    float s[NT][4];
+    // ---- S^T = K * Q^T, one m-tile per 16 keys ------------------------------
+    // s / s2: two independent accumulation chains per m-tile (even / odd
+    // k-steps) halve the dependent-MMA latency.
+    float s[KST][NT][4], s2[KST][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) s[nt][c] = 0.f;
-    if constexpr (!INT8) {
-      // two independent accumulation chains halve the dependent-MMA latency
-      float s2[NT][4];
+    for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s2[nt][c] = 0.f;
+        for (int c = 0; c < 4; ++c) s[mk][nt][c] = s2[mk][nt][c] = 0.f;
+    if constexpr (!INT8) {
       const int j = lane >> 3;
       const int row = (lane & 7) + 8 * (j & 1);
 #pragma unroll
-      for (int kk = 0; kk < KS; ++kk) {
-        uint32_t a[4];
-        ldsm_x4(sk + toff<C::ROWB>(row, 2 * kk + (j >> 1)), a[0], a[1], a[2], a[3]);
+      for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          if (kk & 1) mma16816<MMA_BF16>(s2[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
-          else mma16816<MMA_BF16>(s[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+        for (int kk = 0; kk < KS; ++kk) {
+          uint32_t a[4];
+          ldsm_x4(sk + toff<C::ROWB, TK>(row + 16 * mk, 2 * kk + (j >> 1)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if (kk & 1) mma16816<MMA_BF16>(s2[mk][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+            else mma16816<MMA_BF16>(s[mk][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+          }
         }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) s[nt][c] += s2[nt][c];
     } else {
-      float s2[NT][4];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) s2[nt][c] = 0.f;
 #pragma unroll
       for (int gg = 0; gg < D / 64; ++gg) {
         const int chn = 4 * gg + q4;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB>(r, chn));
-        const uint4 w1 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB>(r + 8, chn));
-        const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w};
-        const uint32_t x1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          uint32_t a[4];
-          i8x4_to_f16x4(x0[jj], a[0], a[2]);
-          i8x4_to_f16x4(x1[jj], a[1], a[3]);
+        for (int mk = 0; mk < KST; ++mk) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB, TK>(r + 16 * mk, chn));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB, TK>(r + 8 + 16 * mk, chn));
+          const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t x1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if (jj & 1) mma16816<false>(s2[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
-            else mma16816<false>(s[nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+          for (int jj = 0; jj < 4; ++jj) {
+            uint32_t a[4];
+            i8x4_to_f16x4(x0[jj], a[0], a[2]);
+            i8x4_to_f16x4(x1[jj], a[1], a[3]);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (jj & 1) mma16816<false>(s2[mk][nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+              else mma16816<false>(s[mk][nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
+            }
           }
         }
       }
+    }
+#pragma unroll
+    for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s[nt][c] += s2[nt][c];
-    }
+        for (int c = 0; c < 4; ++c) s[mk][nt][c] += s2[mk][nt][c];
 
-    // ---- scales (INT8) --------------------------------------------------
-    float ksc0 = 1.f, ksc1 = 1.f, vsc0 = 1.f, vsc1 = 1.f;
-    if constexpr (INT8) {
-      const uint32_t* sw = reinterpret_cast<const uint32_t*>(sc);
-      const unsigned hm = reinterpret_cast<const unsigned*>(sc + 128)[0];
-      ksc0 = scale_from_word(sw[r], (hm >> r) & 1, p.scale_f32);
-      ksc1 = scale_from_word(sw[r + 8], (hm >> (r + 8)) & 1, p.scale_f32);
-      vsc0 = scale_from_word(sw[16 + r], (hm >> (16 + r)) & 1, p.scale_f32);
-      vsc1 = scale_from_word(sw[24 + r], (hm >> (24 + r)) & 1, p.scale_f32);
-    }
+    // ---- scales (INT8): rows r + 8*hh + 16*mk ------------------------------
+    float ksc[KST][2], vsc[KST][2];
+#pragma unroll
+    for (int mk = 0; mk < KST; ++mk)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        ksc[mk][hh] = 1.f;
+        vsc[mk][hh] = 1.f;
+        if constexpr (INT8) {
+          const uint32_t* sw = reinterpret_cast<const uint32_t*>(sc);
+          const int row = r + 8 * hh + 16 * mk;
+          ksc[mk][hh] = scale_from_word(sw[row], (meta[0] >> row) & 1, p.scale_f32);
+          vsc[mk][hh] = scale_from_word(sw[TK + row], (meta[2] >> row) & 1, p.scale_f32);
+        }
+      }
 
     // ---- online softmax (base 2) ------------------------------------------
-    const int key_a = cp.tile * TILE + r;
-    const int key_b = key_a + 8;
+    const int key_r = cp.tile * TK + r;
     uint32_t* pw = reinterpret_cast<uint32_t*>(pbuf);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      float pv[4];
+      float pv[KST][4];
       float alpha[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float x0 = s[nt][e] * ksc0 * p.scale_log2;
-        float x1 = s[nt][2 + e] * ksc1 * p.scale_log2;
-        if (key_a >= lim[nt][e]) x0 = -INFINITY;
-        if (key_b >= lim[nt][e]) x1 = -INFINITY;
-        const float tmax = warp_max_xor(fmaxf(x0, x1), 4);
+        float x[KST][2];
+        float tm = -INFINITY;
+#pragma unroll
+        for (int mk = 0; mk < KST; ++mk)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float v = s[mk][nt][e + 2 * hh] * ksc[mk][hh] * p.scale_log2;
+            if (key_r + 16 * mk + 8 * hh >= lim[nt][e]) v = -INFINITY;
+            x[mk][hh] = v;
+            tm = fmaxf(tm, v);
+          }
+        const float tmax = warp_max_xor(tm, 4);
         const float m_new = fmaxf(m_run[nt][e], tmax);
         const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
         alpha[e] = ex2(m_run[nt][e] - m_use);
-        const float p0 = ex2(x0 - m_use);
-        const float p1 = ex2(x1 - m_use);
-        l_run[nt][e] = l_run[nt][e] * alpha[e] + p0 + p1;
+        float ps = 0.f;
+#pragma unroll
+        for (int mk = 0; mk < KST; ++mk)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float pe = ex2(x[mk][hh] - m_use);
+            pv[mk][e + 2 * hh] = pe;
+            ps += pe;
+          }
+        l_run[nt][e] = l_run[nt][e] * alpha[e] + ps;
         m_run[nt][e] = m_new;
-        pv[e] = p0;
-        pv[2 + e] = p1;
       }
       // alpha == 1 for every column of the warp: the running max did not move
       if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
@@ -591,19 +680,28 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
         }
       }
       // P^T tile [key][col] (fp16 or bf16, V scale folded in for INT8)
-      pw[(r * NC + nt * 8 + 2 * q4) >> 1] = pack2<MMA_BF16>(pv[0] * vsc0, pv[1] * vsc0);
-      pw[((r + 8) * NC + nt * 8 + 2 * q4) >> 1] = pack2<MMA_BF16>(pv[2] * vsc1, pv[3] * vsc1);
+#pragma unroll
+      for (int mk = 0; mk < KST; ++mk) {
+        pw[((r + 16 * mk) * NC + nt * 8 + 2 * q4) >> 1] =
+            pack2<MMA_BF16>(pv[mk][0] * vsc[mk][0], pv[mk][1] * vsc[mk][0]);
+        pw[((r + 8 + 16 * mk) * NC + nt * 8 + 2 * q4) >> 1] =
+            pack2<MMA_BF16>(pv[mk][2] * vsc[mk][1], pv[mk][3] * vsc[mk][1]);
+      }
     }
     __syncwarp();
-    uint32_t bp[NT][2];
+    uint32_t bp[KST][NT][2];
     {
       const uint32_t pb = smem_u32(pbuf);
       if constexpr (NT == 1) {
-        ldsm_x2_t(pb + (lane & 15) * NC * 2, bp[0][0], bp[0][1]);
+        if constexpr (KST == 1) ldsm_x2_t(pb + (lane & 15) * NC * 2, bp[0][0][0], bp[0][0][1]);
+        else ldsm_x4_t(pb + lane * NC * 2, bp[0][0][0], bp[0][0][1], bp[1][0][0], bp[1][0][1]);
       } else {
-        const int row = lane & 15;
-        const int colb = (lane >> 4) * 8;
-        ldsm_x4_t(pb + (row * NC + colb) * 2, bp[0][0], bp[0][1], bp[1][0], bp[1][1]);
+#pragma unroll
+        for (int mk = 0; mk < KST; ++mk) {
+          const int row = (lane & 15) + 16 * mk;
+          const int colb = (lane >> 4) * 8;
+          ldsm_x4_t(pb + (row * NC + colb) * 2, bp[mk][0][0], bp[mk][0][1], bp[mk][1][0], bp[mk][1][1]);
+        }
       }
     }
 
@@ -612,45 +710,50 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
       const int j = lane >> 3;
       const int row = (lane & 7) + 8 * (j >> 1);
 #pragma unroll
-      for (int mt = 0; mt < KS; ++mt) {
-        uint32_t a[4];
-        ldsm_x4_t(sv + toff<C::ROWB>(row, 2 * mt + (j & 1)), a[0], a[1], a[2], a[3]);
+      for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(acc[mt][nt], a, bp[nt][0], bp[nt][1]);
-      }
+        for (int mt = 0; mt < KS; ++mt) {
+          uint32_t a[4];
+          ldsm_x4_t(sv + toff<C::ROWB, TK>(row + 16 * mk, 2 * mt + (j & 1)), a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma16816<MMA_BF16>(acc[mt][nt], a, bp[mk][nt][0], bp[mk][nt][1]);
+        }
     } else {
       constexpr int WORDS = D / 32;  // 32-bit words of this thread's d range per key
-      uint32_t R[4][WORDS];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int row = 2 * q4 + (c & 1) + 8 * (c >> 1);
-        if constexpr (D >= 128) {
-          const uint4 w = *reinterpret_cast<const uint4*>(vt + toff<C::ROWB>(row, r));
-          R[c][0] = w.x;
-          R[c][1] = w.y;
-          R[c][2] = w.z;
-          R[c][3] = w.w;
-        } else {
-          const uint2 w = *reinterpret_cast<const uint2*>(vt + toff<C::ROWB>(row, r >> 1) + (r & 1) * 8);
-          R[c][0] = w.x;
-          R[c][1] = w.y;
+      for (int mk = 0; mk < KST; ++mk) {
+        uint32_t R[4][WORDS];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int row = 16 * mk + 2 * q4 + (c & 1) + 8 * (c >> 1);
+          if constexpr (D >= 128) {
+            const uint4 w = *reinterpret_cast<const uint4*>(vt + toff<C::ROWB, TK>(row, r));
+            R[c][0] = w.x;
+            R[c][1] = w.y;
+            R[c][2] = w.z;
+            R[c][3] = w.w;
+          } else {
+            const uint2 w = *reinterpret_cast<const uint2*>(vt + toff<C::ROWB, TK>(row, r >> 1) + (r & 1) * 8);
+            R[c][0] = w.x;
+            R[c][1] = w.y;
+          }
         }
-      }
 #pragma unroll
-      for (int w = 0; w < WORDS; ++w) {
-        const uint32_t x01 = prmt(R[0][w], R[1][w], 0x5140u);
-        const uint32_t y01 = prmt(R[0][w], R[1][w], 0x7362u);
-        const uint32_t x23 = prmt(R[2][w], R[3][w], 0x5140u);
-        const uint32_t y23 = prmt(R[2][w], R[3][w], 0x7362u);
-        uint32_t a[4], b2[4];
-        i8x4_to_f16x4(x01, a[0], a[1]);
-        i8x4_to_f16x4(x23, a[2], a[3]);
-        i8x4_to_f16x4(y01, b2[0], b2[1]);
-        i8x4_to_f16x4(y23, b2[2], b2[3]);
+        for (int w = 0; w < WORDS; ++w) {
+          const uint32_t x01 = prmt(R[0][w], R[1][w], 0x5140u);
+          const uint32_t y01 = prmt(R[0][w], R[1][w], 0x7362u);
+          const uint32_t x23 = prmt(R[2][w], R[3][w], 0x5140u);
+          const uint32_t y23 = prmt(R[2][w], R[3][w], 0x7362u);
+          uint32_t a[4], b2[4];
+          i8x4_to_f16x4(x01, a[0], a[1]);
+          i8x4_to_f16x4(x23, a[2], a[3]);
+          i8x4_to_f16x4(y01, b2[0], b2[1]);
+          i8x4_to_f16x4(y23, b2[2], b2[3]);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          mma16816<false>(acc[2 * w][nt], a, bp[nt][0], bp[nt][1]);
-          mma16816<false>(acc[2 * w + 1][nt], b2, bp[nt][0], bp[nt][1]);
+          for (int nt = 0; nt < NT; ++nt) {
+            mma16816<false>(acc[2 * w][nt], a, bp[mk][nt][0], bp[mk][nt][1]);
+            mma16816<false>(acc[2 * w + 1][nt], b2, bp[mk][nt][0], bp[mk][nt][1]);
+          }
         }
       }
     }
