@@ -339,6 +339,8 @@ int build_write(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_
   if (nw->dtype != PA_DTYPE_F16 && nw->dtype != PA_DTYPE_BF16 && nw->dtype != PA_DTYPE_F32)
     return fail(PA_ERR_INVALID, "new K/V dtype must be fp16, bf16 or fp32");
   if (nw->num_tokens < 0) return fail(PA_ERR_INVALID, "num_tokens < 0");
+  if (static_cast<long long>(nw->num_tokens) * kv->num_kv_heads > (1LL << 26))
+    return fail(PA_ERR_UNSUPPORTED, "write of more than 2^26 (token, kv head) rows in one call");
   const int e = elt_size(nw->dtype);
   if (nw->num_tokens > 0) {
     if (!nw->k_new || !nw->v_new || !nw->seq_index || !nw->positions || !pg->block_table)

@@ -448,6 +448,11 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   float acc[KS][NT][4];
   float m_run[NT][2], l_run[NT][2];
   int lim[NT][2];
+  int lim_min = 0;      // fewest visible keys over the warp's columns (warp-uniform)
+  // INT8 (biased operands): I8_BIAS * sum_d q_d of this thread's S columns, and
+  // the per-column sum of P' accumulated by an MMA with an all-ones A operand.
+  float qs[NT][2];
+  float acc1[NT][4];
   int piece_start_tile = 0;
   int qlen_b = 0;
   bool piece_first = true;  // first piece of this warp's range
@@ -529,6 +534,31 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int c = 0; c < 4; ++c) acc[mt][nt][c] = 0.f;
+      int lm = lim[0][0];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) lm = min(lm, min(lim[nt][0], lim[nt][1]));
+      lim_min = __reduce_min_sync(0xffffffffu, lm);
+      if constexpr (INT8) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          // this thread's Q fragments are column nt*8 + r; sum over the four
+          // threads of the row group gives the column's sum over head_dim
+          float part = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qf[nt][kk][hf]));
+              part += f.x + f.y;
+            }
+          part += __shfl_xor_sync(0xffffffffu, part, 1);
+          part += __shfl_xor_sync(0xffffffffu, part, 2);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) qs[nt][e] = I8_BIAS * __shfl_sync(0xffffffffu, part, (2 * q4 + e) << 2);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc1[nt][c] = 0.f;
+        }
+      }
     }
 
     // ---- wait for this tile ----------------------------------------------
@@ -599,8 +629,8 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             uint32_t a[4];
-            i8x4_to_f16x4(x0[jj], a[0], a[2]);
-            i8x4_to_f16x4(x1[jj], a[1], a[3]);
+            i8x4_to_f16x4_biased(x0[jj], a[0], a[2]);
+            i8x4_to_f16x4_biased(x1[jj], a[1], a[3]);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               if (jj & 1) mma16816<false>(s2[mk][nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj][1]);
@@ -617,67 +647,89 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) s[mk][nt][c] += s2[mk][nt][c];
 
-    // ---- scales (INT8): rows r + 8*hh + 16*mk ------------------------------
-    float ksc[KST][2], vsc[KST][2];
+    // ---- per-row logit multiplier (K scale x softmax scale) and V scale -----
+    // rows r + 8*hh + 16*mk
+    float kscl[KST][2], vsc[KST][2];
 #pragma unroll
     for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        ksc[mk][hh] = 1.f;
+        kscl[mk][hh] = p.scale_log2;
         vsc[mk][hh] = 1.f;
         if constexpr (INT8) {
           const uint32_t* sw = reinterpret_cast<const uint32_t*>(sc);
           const int row = r + 8 * hh + 16 * mk;
-          ksc[mk][hh] = scale_from_word(sw[row], (meta[0] >> row) & 1, p.scale_f32);
+          kscl[mk][hh] = scale_from_word(sw[row], (meta[0] >> row) & 1, p.scale_f32) * p.scale_log2;
           vsc[mk][hh] = scale_from_word(sw[TK + row], (meta[2] >> row) & 1, p.scale_f32);
         }
       }
 
     // ---- online softmax (base 2) ------------------------------------------
+    // The reference max of a column only moves when a logit exceeds it by
+    // more than 2^8 (or on the piece's first tile): P stays <= 256, and most
+    // tiles skip the cross-lane max, the alpha exponentials and the rescale.
     const int key_r = cp.tile * TK + r;
+    const bool full = (cp.tile + 1) * TK <= lim_min;  // every key of the tile visible to every column
     uint32_t* pw = reinterpret_cast<uint32_t*>(pbuf);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       float pv[KST][4];
-      float alpha[2];
+      float x[2][KST][2];
+      float tm[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float x[KST][2];
-        float tm = -INFINITY;
+        tm[e] = -INFINITY;
 #pragma unroll
         for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            float v = s[mk][nt][e + 2 * hh] * ksc[mk][hh] * p.scale_log2;
-            if (key_r + 16 * mk + 8 * hh >= lim[nt][e]) v = -INFINITY;
-            x[mk][hh] = v;
-            tm = fmaxf(tm, v);
+            float sv = s[mk][nt][e + 2 * hh];
+            if constexpr (INT8) sv -= qs[nt][e];
+            float v = sv * kscl[mk][hh];
+            if (!full && key_r + 16 * mk + 8 * hh >= lim[nt][e]) v = -INFINITY;
+            x[e][mk][hh] = v;
+            tm[e] = fmaxf(tm[e], v);
           }
-        const float tmax = warp_max_xor(tm, 4);
-        const float m_new = fmaxf(m_run[nt][e], tmax);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        alpha[e] = ex2(m_run[nt][e] - m_use);
+      }
+      if (!__all_sync(0xffffffffu, tm[0] <= m_run[nt][0] + 8.f && tm[1] <= m_run[nt][1] + 8.f)) {
+        float alpha[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float m_new = fmaxf(m_run[nt][e], warp_max_xor(tm[e], 4));
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          alpha[e] = ex2(m_run[nt][e] - m_use);
+          l_run[nt][e] *= alpha[e];
+          m_run[nt][e] = m_new;
+        }
+        if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            acc[mt][nt][0] *= alpha[0];
+            acc[mt][nt][1] *= alpha[1];
+            acc[mt][nt][2] *= alpha[0];
+            acc[mt][nt][3] *= alpha[1];
+          }
+          if constexpr (INT8) {
+            acc1[nt][0] *= alpha[0];
+            acc1[nt][1] *= alpha[1];
+            acc1[nt][2] *= alpha[0];
+            acc1[nt][3] *= alpha[1];
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float m_use = (m_run[nt][e] == -INFINITY) ? 0.f : m_run[nt][e];
         float ps = 0.f;
 #pragma unroll
         for (int mk = 0; mk < KST; ++mk)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const float pe = ex2(x[mk][hh] - m_use);
+            const float pe = ex2(x[e][mk][hh] - m_use);
             pv[mk][e + 2 * hh] = pe;
             ps += pe;
           }
-        l_run[nt][e] = l_run[nt][e] * alpha[e] + ps;
-        m_run[nt][e] = m_new;
-      }
-      // alpha == 1 for every column of the warp: the running max did not move
-      if (!__all_sync(0xffffffffu, alpha[0] == 1.f && alpha[1] == 1.f)) {
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-          acc[mt][nt][0] *= alpha[0];
-          acc[mt][nt][1] *= alpha[1];
-          acc[mt][nt][2] *= alpha[0];
-          acc[mt][nt][3] *= alpha[1];
-        }
+        l_run[nt][e] += ps;
       }
       // P^T tile [key][col] (fp16 or bf16, V scale folded in for INT8)
 #pragma unroll
@@ -745,22 +797,35 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
           const uint32_t x23 = prmt(R[2][w], R[3][w], 0x5140u);
           const uint32_t y23 = prmt(R[2][w], R[3][w], 0x7362u);
           uint32_t a[4], b2[4];
-          i8x4_to_f16x4(x01, a[0], a[1]);
-          i8x4_to_f16x4(x23, a[2], a[3]);
-          i8x4_to_f16x4(y01, b2[0], b2[1]);
-          i8x4_to_f16x4(y23, b2[2], b2[3]);
+          i8x4_to_f16x4_biased(x01, a[0], a[1]);
+          i8x4_to_f16x4_biased(x23, a[2], a[3]);
+          i8x4_to_f16x4_biased(y01, b2[0], b2[1]);
+          i8x4_to_f16x4_biased(y23, b2[2], b2[3]);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             mma16816<false>(acc[2 * w][nt], a, bp[mk][nt][0], bp[mk][nt][1]);
             mma16816<false>(acc[2 * w + 1][nt], b2, bp[mk][nt][0], bp[mk][nt][1]);
           }
         }
+        // sum over keys of P' per column, accumulated exactly like O'
+        const uint32_t ones[4] = {0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u};
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816<false>(acc1[nt], ones, bp[mk][nt][0], bp[mk][nt][1]);
       }
     }
 
     // ---- end of a piece: final output or split-K partial ------------------
     if (pend) {
       const bool complete = (piece_start_tile == 0) && (cp.tile == cp.nt - 1);
+      if constexpr (INT8) {
+        // O' = O + I8_BIAS * sum_k P'_k per column
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[mt][nt][c] -= I8_BIAS * acc1[nt][c & 1];
+      }
       const int slot = piece_first ? 2 * gw : 2 * gw + 1;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {

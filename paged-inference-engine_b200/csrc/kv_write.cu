@@ -11,139 +11,138 @@
 //   q_d    = clamp(round_half_even(x_d / scale), -127, 127)
 //                                     (tests/pre_quantize_test.py:11,
 //                                      transformer/model.py:105-114)
-// The division is the correctly rounded __fdiv_rn and the rounding is
-// __float2int_rn, so the int8 values are bit-identical to torch's
-// round(x / scale).clamp(-127, 127) on the same fp32 inputs.  The stored scale
-// is `scale` rounded to the pool's scale dtype (fp16 RNE, or fp32 exactly).
+// scale is the correctly rounded __fdiv_rn, and each q_d equals
+// __float2int_rn(__fdiv_rn(x_d, scale)) (quant_row_fast below), so the int8
+// values are bit-identical to torch's round(x / scale).clamp(-127, 127) on the
+// same fp32 inputs.  The stored scale is `scale` rounded to the pool's scale
+// dtype (fp16 RNE, or fp32 exactly).
 #include "pa_common.cuh"
 
 namespace pa {
 namespace {
 
-// Load EPL consecutive elements of the input dtype into fp32.
-template <int EPL, int IN>
-__device__ __forceinline__ void load_row(const void* base, float (&f)[EPL]) {
+// Per-warp geometry for one (input dtype, head_dim): every lane loads 16
+// bytes per instruction, LPR lanes cover one row, and a warp owns the K and V
+// rows of HG kv heads of one token (NL loads per lane in flight at once).
+template <int IN, int D>
+struct WCfg {
+  static constexpr int ESZ = IN == PA_DTYPE_F32 ? 4 : 2;
+  static constexpr int EPL = 16 / ESZ;   // elements per lane per load
+  static constexpr int LPR = D / EPL;    // lanes per row
+  static constexpr int RPI = 32 / LPR;   // rows per load instruction
+  static constexpr int NL = 8;           // loads per lane
+  static constexpr int HG = NL * RPI / 2;  // kv heads per warp (K and V rows)
+  static_assert(LPR >= 1 && LPR <= 32 && 32 % LPR == 0, "row must map onto whole lanes");
+};
+
+template <int IN, int EPL>
+__device__ __forceinline__ void unpack_row(const uint4& w, float (&f)[EPL]) {
   if constexpr (IN == PA_DTYPE_F32) {
-    const float4* p = static_cast<const float4*>(base);
-    if constexpr (EPL == 2) {
-      float2 v = *static_cast<const float2*>(base);
-      f[0] = v.x;
-      f[1] = v.y;
-    } else {
-#pragma unroll
-      for (int i = 0; i < EPL / 4; ++i) {
-        float4 v = p[i];
-        f[4 * i + 0] = v.x;
-        f[4 * i + 1] = v.y;
-        f[4 * i + 2] = v.z;
-        f[4 * i + 3] = v.w;
-      }
-    }
+    f[0] = __uint_as_float(w.x);
+    f[1] = __uint_as_float(w.y);
+    f[2] = __uint_as_float(w.z);
+    f[3] = __uint_as_float(w.w);
   } else {
-    uint32_t w[EPL / 2];
-    if constexpr (EPL == 2) {
-      w[0] = *static_cast<const uint32_t*>(base);
-    } else if constexpr (EPL == 4) {
-      uint2 v = *static_cast<const uint2*>(base);
-      w[0] = v.x;
-      w[1] = v.y;
-    } else {
-      uint4 v = *static_cast<const uint4*>(base);
-      w[0] = v.x;
-      w[1] = v.y;
-      w[2] = v.z;
-      w[3] = v.w;
-    }
+    const uint32_t x[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int i = 0; i < EPL / 2; ++i) {
-      if constexpr (IN == PA_DTYPE_BF16) {
-        float2 x = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[i]));
-        f[2 * i] = x.x;
-        f[2 * i + 1] = x.y;
-      } else {
-        float2 x = __half22float2(*reinterpret_cast<__half2*>(&w[i]));
-        f[2 * i] = x.x;
-        f[2 * i + 1] = x.y;
-      }
+    for (int i = 0; i < 4; ++i) {
+      float2 v;
+      if constexpr (IN == PA_DTYPE_BF16) v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x[i]));
+      else v = __half22float2(*reinterpret_cast<const __half2*>(&x[i]));
+      f[2 * i] = v.x;
+      f[2 * i + 1] = v.y;
     }
   }
+}
+
+// round_half_even(x / s) for |x| <= 127 * s, as the low byte of an fp32 sum.
+// inv = rcp.approx(s) (at most 1 ulp off, per the PTX ISA; a relative error
+// below 2^-22 is all this needs) and y = x * inv differs from x / s by at most
+// |x / s| * (2^-22 + 2^-24), and from the correctly rounded quotient
+// fl(x / s) by at most that plus half an ulp of fl(x / s): below 4.3e-5 for
+// |x / s| <= 127.  Unless y lies within 1e-4 of a half-integer both round to
+// the same integer; rows where some value does are redone with the exact
+// division (quant_row_exact).  Adding 1.5 * 2^23 rounds to the nearest
+// integer, ties to even, and leaves it in the low mantissa bits, whose low
+// byte is the int8 two's complement encoding.  No clamp is needed:
+// |x| <= absmax gives |fl(x / s)| <= 127 * (1 + 2^-23) and
+// |y| <= 127 * (1 + 2^-21), both rounding to at most 127 in magnitude.
+constexpr float RNE_MAGIC = 12582912.0f;  // 1.5 * 2^23
+constexpr float NEAR_HALF = 0.5f - 1.0e-4f;
+
+__device__ __forceinline__ uint32_t q_byte(float y) { return __float_as_uint(y + RNE_MAGIC); }
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Four quotient bytes (low bytes of b0..b3) -> one int8x4 word.
+__device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+  return prmt(prmt(b0, b1, 0x0040u), prmt(b2, b3, 0x0040u), 0x5410u);
 }
 
 template <int EPL>
-__device__ __forceinline__ void store_i8(void* dst, const int (&q)[EPL]) {
-  uint32_t w[(EPL + 3) / 4] = {};
+__device__ __forceinline__ bool quant_row_fast(const float (&f)[EPL], float inv, uint32_t (&w)[EPL / 4]) {
+  bool near = false;
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) w[i / 4] |= (static_cast<uint32_t>(q[i]) & 0xffu) << (8 * (i % 4));
-  if constexpr (EPL == 2) {
-    *static_cast<unsigned short*>(dst) = static_cast<unsigned short>(w[0]);
-  } else if constexpr (EPL == 4) {
-    *static_cast<uint32_t*>(dst) = w[0];
-  } else {
-    *static_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-  }
-}
-
-template <int EPL, bool BF16>
-__device__ __forceinline__ void store_16b(void* dst, const float (&f)[EPL]) {
-  uint32_t w[EPL / 2];
+  for (int i = 0; i < EPL / 4; ++i) {
+    uint32_t b[4];
 #pragma unroll
-  for (int i = 0; i < EPL / 2; ++i) w[i] = pack2<BF16>(f[2 * i], f[2 * i + 1]);
-  if constexpr (EPL == 2) {
-    *static_cast<uint32_t*>(dst) = w[0];
-  } else if constexpr (EPL == 4) {
-    *static_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-  } else {
-    *static_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int k = 0; k < 4; ++k) {
+      const float y = f[4 * i + k] * inv;
+      const float r = (y + RNE_MAGIC) - RNE_MAGIC;
+      near |= fabsf(y - r) > NEAR_HALF;
+      b[k] = q_byte(y);
+    }
+    w[i] = pack_bytes(b[0], b[1], b[2], b[3]);
   }
+  return near;
 }
 
 template <int EPL>
-__device__ __forceinline__ void write_row(const WriteParams& p, const void* src, void* cache_row, void* scale_ptr,
-                                          int lane) {
-  float f[EPL];
-  const int off = lane * EPL;
-  switch (p.in_dtype) {
-    case PA_DTYPE_F32:
-      load_row<EPL, PA_DTYPE_F32>(static_cast<const float*>(src) + off, f);
-      break;
-    case PA_DTYPE_BF16:
-      load_row<EPL, PA_DTYPE_BF16>(static_cast<const __nv_bfloat16*>(src) + off, f);
-      break;
-    default:
-      load_row<EPL, PA_DTYPE_F16>(static_cast<const __half*>(src) + off, f);
-      break;
-  }
-  if (p.cache_dtype == PA_DTYPE_I8) {
-    float amax = 0.f;
+__device__ __noinline__ void quant_row_exact(const float (&f)[EPL], float s, uint32_t (&w)[EPL / 4]) {
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(f[i]));
-    amax = warp_max_xor(amax, 1);
-    const float scale = (amax == 0.f) ? 1.0f : __fdiv_rn(amax, 127.0f);
-    int q[EPL];
+  for (int i = 0; i < EPL / 4; ++i) {
+    uint32_t b[4];
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      int v = __float2int_rn(__fdiv_rn(f[i], scale));
-      q[i] = max(-127, min(127, v));
-    }
-    store_i8<EPL>(static_cast<int8_t*>(cache_row) + off, q);
-    if (lane == 0) {
-      if (p.scale_f32) *static_cast<float*>(scale_ptr) = scale;
-      else *static_cast<__half*>(scale_ptr) = __float2half_rn(scale);
-    }
-  } else if (p.cache_dtype == PA_DTYPE_BF16) {
-    store_16b<EPL, true>(static_cast<__nv_bfloat16*>(cache_row) + off, f);
-  } else {
-    store_16b<EPL, false>(static_cast<__half*>(cache_row) + off, f);
+    for (int k = 0; k < 4; ++k) b[k] = q_byte(__fdiv_rn(f[4 * i + k], s));
+    w[i] = pack_bytes(b[0], b[1], b[2], b[3]);
   }
 }
 
-template <int EPL>
+// Quantise-on-write / copy-on-write.  One warp per (token, group of HG kv
+// heads): the group's K and V source rows are loaded before the token's
+// block-table entry is known, so the index lookups overlap the row loads.
+template <int IN, int D>
 __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
+  using C = WCfg<IN, D>;
+  constexpr int EPL = C::EPL;
   const int lane = threadIdx.x & 31;
-  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (row >= static_cast<long long>(p.T) * p.Hkv) return;
-  const int t = static_cast<int>(row / p.Hkv);
-  const int h = static_cast<int>(row % p.Hkv);
+  const int wid = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int groups = (p.Hkv + C::HG - 1) / C::HG;
+  if (wid >= p.T * groups) return;  // T * groups < 2^26 (checked on the host)
+  const int t = groups == 1 ? wid : wid / groups;
+  const int h0 = (wid - t * groups) * C::HG;
+  const int part = lane % C::LPR;
+  const int sub = lane / C::LPR;
+
+  // ---- 1. source rows (row j of the warp: head h0 + j/2, K for even j) ----
+  uint4 raw[C::NL];
+#pragma unroll
+  for (int it = 0; it < C::NL; ++it) {
+    const int j = it * C::RPI + sub;
+    const int h = h0 + (j >> 1);
+    raw[it] = make_uint4(0, 0, 0, 0);
+    if (h < p.Hkv) {
+      const char* src = (j & 1) ? static_cast<const char*>(p.v_new) + (t * p.vn_st + h * p.vn_sh) * C::ESZ
+                                : static_cast<const char*>(p.k_new) + (t * p.kn_st + h * p.kn_sh) * C::ESZ;
+      raw[it] = __ldg(reinterpret_cast<const uint4*>(src) + part);
+    }
+  }
+
+  // ---- 2. destination block / slot ----------------------------------------
   const int s = p.seq_idx[t];
   const int pos = p.pos[t];
   if (s < 0 || s >= p.num_seqs) {
@@ -161,45 +160,83 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
     return;
   }
   const int slot = pos & (p.BS - 1);
-  const int esz = p.in_dtype == PA_DTYPE_F32 ? 4 : 2;
-  const int csz = p.cache_dtype == PA_DTYPE_I8 ? 1 : 2;
+  const long long kb = blk * p.k_sblk + slot * p.k_sslot, vb = blk * p.v_sblk + slot * p.v_sslot;
+  const long long ksb = blk * p.ks_sblk + slot * p.ks_sslot, vsb = blk * p.vs_sblk + slot * p.vs_sslot;
 
-  const char* ksrc = static_cast<const char*>(p.k_new) + (t * p.kn_st + h * p.kn_sh) * esz;
-  const char* vsrc = static_cast<const char*>(p.v_new) + (t * p.vn_st + h * p.vn_sh) * esz;
-  char* kdst = static_cast<char*>(p.k) + (blk * p.k_sblk + slot * p.k_sslot + h * p.k_shead) * csz;
-  char* vdst = static_cast<char*>(p.v) + (blk * p.v_sblk + slot * p.v_sslot + h * p.v_shead) * csz;
-  void* ksc = nullptr;
-  void* vsc = nullptr;
-  if (p.cache_dtype == PA_DTYPE_I8) {
-    const int ssz = p.scale_f32 ? 4 : 2;
-    ksc = static_cast<char*>(p.ks) + (blk * p.ks_sblk + slot * p.ks_sslot + h * p.ks_shead) * ssz;
-    vsc = static_cast<char*>(p.vs) + (blk * p.vs_sblk + slot * p.vs_sslot + h * p.vs_shead) * ssz;
+  // ---- 3. convert and store -------------------------------------------------
+#pragma unroll
+  for (int it = 0; it < C::NL; ++it) {
+    const int j = it * C::RPI + sub;
+    const int h = h0 + (j >> 1);
+    const bool isv = j & 1;
+    const bool live = h < p.Hkv;
+    float f[EPL];
+    unpack_row<IN, EPL>(raw[it], f);
+    const long long row = isv ? vb + h * p.v_shead : kb + h * p.k_shead;
+    if (p.cache_dtype == PA_DTYPE_I8) {
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+      for (int o = C::LPR / 2; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = (amax == 0.f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+      uint32_t w[EPL / 4];
+      const bool near = quant_row_fast<EPL>(f, rcp_approx(sc), w);
+      if (__any_sync(0xffffffffu, near)) quant_row_exact<EPL>(f, sc, w);
+      if (live) {
+        int8_t* dst = static_cast<int8_t*>(isv ? p.v : p.k) + row + part * EPL;
+        if constexpr (EPL == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+        else *reinterpret_cast<uint32_t*>(dst) = w[0];
+        if (part == 0) {
+          const long long so = isv ? vsb + h * p.vs_shead : ksb + h * p.ks_shead;
+          void* sp = isv ? p.vs : p.ks;
+          if (p.scale_f32) static_cast<float*>(sp)[so] = sc;
+          else static_cast<__half*>(sp)[so] = __float2half_rn(sc);
+        }
+      }
+    } else if (live) {
+      const bool bf = p.cache_dtype == PA_DTYPE_BF16;
+      uint16_t* dst = static_cast<uint16_t*>(isv ? p.v : p.k) + row + part * EPL;
+      if constexpr (IN == PA_DTYPE_F16 || IN == PA_DTYPE_BF16) {
+        if ((IN == PA_DTYPE_BF16) == bf) {
+          *reinterpret_cast<uint4*>(dst) = raw[it];  // same 16-bit type: plain copy
+          continue;
+        }
+      }
+      uint32_t w[EPL / 2];
+#pragma unroll
+      for (int i = 0; i < EPL / 2; ++i) w[i] = bf ? pack2<true>(f[2 * i], f[2 * i + 1]) : pack2<false>(f[2 * i], f[2 * i + 1]);
+      if constexpr (EPL == 8) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    }
   }
-  write_row<EPL>(p, ksrc, kdst, ksc, lane);
-  write_row<EPL>(p, vsrc, vdst, vsc, lane);
+}
+
+template <int IN>
+cudaError_t launch_in(const WriteParams& p, cudaStream_t stream) {
+  auto go = [&](auto kern, int hg) {
+    const long long warps = static_cast<long long>(p.T) * ((p.Hkv + hg - 1) / hg);
+    const long long blocks = (warps * 32 + 255) / 256;
+    kern<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+    return cudaGetLastError();
+  };
+  if (p.D == 64) return go(kv_write_kernel<IN, 64>, WCfg<IN, 64>::HG);
+  if (p.D == 128) return go(kv_write_kernel<IN, 128>, WCfg<IN, 128>::HG);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace
 
 cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream) {
-  const long long rows = static_cast<long long>(p.T) * p.Hkv;
-  if (rows == 0) return cudaSuccess;
-  const int threads = 256;
-  const long long blocks = (rows * 32 + threads - 1) / threads;
-  switch (p.D) {
-    case 64:
-      kv_write_kernel<2><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-      break;
-    case 128:
-      kv_write_kernel<4><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-      break;
-    case 256:
-      kv_write_kernel<8><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(p);
-      break;
+  if (static_cast<long long>(p.T) * p.Hkv == 0) return cudaSuccess;
+  switch (p.in_dtype) {
+    case PA_DTYPE_F32:
+      return launch_in<PA_DTYPE_F32>(p, stream);
+    case PA_DTYPE_BF16:
+      return launch_in<PA_DTYPE_BF16>(p, stream);
     default:
-      return cudaErrorInvalidValue;
+      return launch_in<PA_DTYPE_F16>(p, stream);
   }
-  return cudaGetLastError();
 }
 
 }  // namespace pa

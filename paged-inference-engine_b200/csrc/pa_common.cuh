@@ -107,6 +107,17 @@ __device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t& lo, uint32_t
   hi = *reinterpret_cast<uint32_t*>(&hb);
 }
 
+// Four signed int8 values -> two packed fp16 pairs holding 1152 + b_i (the
+// byte biased to unsigned and placed in the mantissa of 1024.0h): exact, and
+// one subtraction per pair cheaper than i8x4_to_f16x4.  Callers remove the
+// 1152 offset after the dot product (it adds 1152 * sum of the other operand).
+constexpr float I8_BIAS = 1152.0f;
+__device__ __forceinline__ void i8x4_to_f16x4_biased(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  lo = prmt(u, 0x64646464u, 0x5140u);
+  hi = prmt(u, 0x64646464u, 0x7362u);
+}
+
 __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -174,6 +174,71 @@ def test_random_vs_oracle(fa, cfg, top_left, mode):
     _compare(O, L, O_or, L_or, meta["q_len"].numpy(), tol, f"{cfg}")
 
 
+@pytest.mark.parametrize("kv", ["f16", "i8"])
+@pytest.mark.parametrize("mode", ["decode", "prefill"])
+def test_rising_logits_vs_oracle(fa, kv, mode):
+    """Key norms that grow ~13x along each sequence: the kernels' reference
+    max has to move again and again (their rescale paths), also inside split-K
+    pieces, and the softmax ends up dominated by a few late keys."""
+    B, Hq, Hkv, D, BS = 3, 8, 2, 128, 16
+    ctx = [300, 1000, 2049]
+    gen = torch.Generator().manual_seed(77)
+    nblk = [-(-c // BS) for c in ctx]
+    NB = sum(nblk)
+    perm = torch.randperm(NB, generator=gen).to(torch.int32)
+    bt = torch.zeros(B, max(nblk), dtype=torch.int32)
+    growth = torch.ones(NB, BS)
+    cur = 0
+    for b, n in enumerate(nblk):
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+        pos = torch.arange(n * BS, dtype=torch.float32).view(n, BS)
+        growth[bt[b, :n].long()] = 1.0 + pos * (12.0 / ctx[b])
+    K16 = torch.randn(NB, BS, Hkv, D, generator=gen) * growth[:, :, None, None]
+    V16 = torch.randn(NB, BS, Hkv, D, generator=gen)
+    Q = torch.randn(B, Hq, 1, D, generator=gen).half()
+    if kv == "i8":
+        kq, ksn = orc.quantize_rows(K16.numpy())
+        vq, vsn = orc.quantize_rows(V16.numpy())
+        ksn, vsn = ksn.astype(np.float16), vsn.astype(np.float16)
+        K, V, ks, vs, Kn, Vn = torch.from_numpy(kq), torch.from_numpy(vq), torch.from_numpy(ksn), \
+            torch.from_numpy(vsn), kq, vq
+    else:
+        K, V = K16.half(), V16.half()
+        ks = vs = ksn = vsn = None
+        Kn, Vn = K.float().numpy(), V.float().numpy()
+    q_len = torch.ones(B, dtype=torch.int32)
+    kv_len = torch.tensor(ctx, dtype=torch.int32)
+    nb = torch.tensor(nblk, dtype=torch.int32)
+    O, L = fa.flash_attention_forward(Q.cuda(), K.cuda(), V.cuda(), q_len.cuda(), bt.cuda(), nb.cuda(), BS,
+                                      kv_len.cuda(), None if ks is None else ks.cuda(),
+                                      None if vs is None else vs.cuda(), mode=mode)
+    torch.cuda.synchronize()
+    O_or, L_or = orc.paged_attention(Q.float().numpy(), Kn, Vn, q_len.numpy(), bt.numpy(), nb.numpy(), BS,
+                                     kv_len.numpy(), ksn, vsn)
+    _compare(O, L, O_or, L_or, q_len.numpy(), TOL_I8 if kv == "i8" else TOL_F16, f"rising {kv} {mode}")
+
+
+def test_repeated_decode_calls_share_one_workspace(fa):
+    """Alternating batch shapes (different grid chunking) through one
+    workspace, three rounds: every call must match the oracle."""
+    cases = []
+    for seed, ctx in ((21, [700, 1, 3000, 45]), (22, [5000, 130]), (23, [17] * 9 + [2500])):
+        Q, K, V, ks, vs, Kn, Vn, ksn, vsn, meta = _random_case(seed, len(ctx), 16, 4, 128, 16, ctx, [1] * len(ctx),
+                                                               torch.int8, torch.float16, "token16")
+        O_or, L_or = orc.paged_attention(Q.float().numpy(), Kn, Vn, meta["q_len"].numpy(),
+                                         meta["block_table"].numpy(), meta["num_blocks"].numpy(), 16,
+                                         meta["kv_len"].numpy(), ksn, vsn)
+        dev = [Q.cuda(), K.cuda(), V.cuda(), meta["q_len"].cuda(), meta["block_table"].cuda(),
+               meta["num_blocks"].cuda(), 16, meta["kv_len"].cuda(), ks.cuda(), vs.cuda()]
+        cases.append((dev, O_or, L_or, meta["q_len"].numpy()))
+    for rep in range(3):
+        for i, (dev, O_or, L_or, ql) in enumerate(cases):
+            O, L = fa.flash_attention_forward(*dev, mode="decode")
+            torch.cuda.synchronize()
+            _compare(O, L, O_or, L_or, ql, TOL_I8, f"call {rep}/{i}")
+
+
 def test_edge_cases(fa):
     """q_len 0, kv_len 0, num_blocks 0 and keys beyond num_blocks*block_size."""
     BS, D, H = 16, 128, 4

@@ -89,6 +89,40 @@ def test_quant_bit_exact_vs_oracle(fa, D, in_dtype, BS):
     assert np.array_equal(vs.cpu().numpy().view(np.uint16), vsn.view(np.uint16))
 
 
+@pytest.mark.parametrize("H", [1, 3, 12])
+@pytest.mark.parametrize("D", [64, 128])
+def test_quant_near_rounding_boundaries(fa, H, D):
+    """Quotients x / scale within a few ulps of k + 0.5, where x * (1 / scale)
+    and the correctly rounded quotient can round to different integers, and
+    head counts that leave a kv-head group of the write kernel partly empty."""
+    T, BS = 64, 16
+    rng = np.random.default_rng(10 * H + D)
+    amax = rng.uniform(0.5, 4.0, size=(T, H)).astype(np.float32)
+    s = (amax / np.float32(127.0)).astype(np.float32)
+    k_int = rng.integers(-126, 126, size=(T, H, D))
+    x = ((k_int + 0.5).astype(np.float32) * s[..., None]).astype(np.float32)
+    x = (x.view(np.int32) + rng.integers(-3, 4, size=x.shape).astype(np.int32)).view(np.float32)
+    x[..., 0] = amax  # the row's absmax, so the scale is amax / 127
+    k = torch.from_numpy(x)
+    v = torch.from_numpy(-x[:, :, ::-1].copy())
+    NB, bt, seq, pos = _layout(T, BS, 2, 4)
+    kc = torch.zeros(NB, BS, H, D, dtype=torch.int8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.zeros(NB, BS, H, dtype=torch.float32, device="cuda")
+    vs = torch.zeros_like(ks)
+    fa.write_kv_cache(k.cuda(), v.cuda(), torch.from_numpy(bt).cuda(), torch.from_numpy(seq).cuda(),
+                      torch.from_numpy(pos).cuda(), kc, vc, ks, vs)
+    torch.cuda.synchronize()
+    kcn = np.zeros((NB, BS, H, D), np.int8)
+    vcn = np.zeros_like(kcn)
+    ksn = np.zeros((NB, BS, H), np.float32)
+    vsn = np.zeros_like(ksn)
+    orc.write_kv_cache(k.numpy(), v.numpy(), bt, seq, pos, kcn, vcn, ksn, vsn, scale_dtype=np.float32)
+    assert np.array_equal(kc.cpu().numpy(), kcn)
+    assert np.array_equal(vc.cpu().numpy(), vcn)
+    assert np.array_equal(ks.cpu().numpy(), ksn) and np.array_equal(vs.cpu().numpy(), vsn)
+
+
 @pytest.mark.parametrize("pool_dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("in_dtype", [torch.float16, torch.bfloat16, torch.float32])
 def test_copy_write_exact(fa, pool_dtype, in_dtype):
