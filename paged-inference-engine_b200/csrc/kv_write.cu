@@ -18,6 +18,10 @@
 // dtype (fp16 RNE, or fp32 exactly).
 #include "pa_common.cuh"
 
+#ifndef PA_WRITE_NL
+#define PA_WRITE_NL 4
+#endif
+
 namespace pa {
 namespace {
 
@@ -30,7 +34,7 @@ struct WCfg {
   static constexpr int EPL = 16 / ESZ;   // elements per lane per load
   static constexpr int LPR = D / EPL;    // lanes per row
   static constexpr int RPI = 32 / LPR;   // rows per load instruction
-  static constexpr int NL = 8;           // loads per lane
+  static constexpr int NL = PA_WRITE_NL;  // loads per lane
   static constexpr int HG = NL * RPI / 2;  // kv heads per warp (K and V rows)
   static_assert(LPR >= 1 && LPR <= 32 && 32 % LPR == 0, "row must map onto whole lanes");
 };
@@ -164,51 +168,82 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
   const long long ksb = blk * p.ks_sblk + slot * p.ks_sslot, vsb = blk * p.vs_sblk + slot * p.vs_sslot;
 
   // ---- 3. convert and store -------------------------------------------------
+  // The NL rows of a lane are independent: each phase runs over all of them
+  // before the next, so their latencies overlap.
+  if (p.cache_dtype == PA_DTYPE_I8) {
+    float am[C::NL];
+#pragma unroll
+    for (int it = 0; it < C::NL; ++it) {
+      float f[EPL];
+      unpack_row<IN, EPL>(raw[it], f);
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) a = fmaxf(a, fabsf(f[i]));
+      am[it] = a;
+    }
+#pragma unroll
+    for (int o = C::LPR / 2; o >= 1; o >>= 1)
+#pragma unroll
+      for (int it = 0; it < C::NL; ++it) am[it] = fmaxf(am[it], __shfl_xor_sync(0xffffffffu, am[it], o));
+    float sc[C::NL];
+    uint32_t w[C::NL][EPL / 4];
+    unsigned near = 0;
+#pragma unroll
+    for (int it = 0; it < C::NL; ++it) {
+      sc[it] = (am[it] == 0.f) ? 1.0f : __fdiv_rn(am[it], 127.0f);
+      float f[EPL];
+      unpack_row<IN, EPL>(raw[it], f);
+      if (quant_row_fast<EPL>(f, rcp_approx(sc[it]), w[it])) near |= 1u << it;
+    }
+    // rows with a quotient near a rounding boundary: redo with the division
+#pragma unroll
+    for (int it = 0; it < C::NL; ++it) {
+      if (__any_sync(0xffffffffu, (near >> it) & 1u)) {
+        float f[EPL];
+        unpack_row<IN, EPL>(raw[it], f);
+        quant_row_exact<EPL>(f, sc[it], w[it]);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < C::NL; ++it) {
+      const int j = it * C::RPI + sub;
+      const int h = h0 + (j >> 1);
+      if (h >= p.Hkv) continue;
+      const bool isv = j & 1;
+      int8_t* dst = static_cast<int8_t*>(isv ? p.v : p.k) + (isv ? vb + h * p.v_shead : kb + h * p.k_shead) + part * EPL;
+      if constexpr (EPL == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[it][0], w[it][1]);
+      else *reinterpret_cast<uint32_t*>(dst) = w[it][0];
+      if (part == 0) {
+        const long long so = isv ? vsb + h * p.vs_shead : ksb + h * p.ks_shead;
+        void* sp = isv ? p.vs : p.ks;
+        if (p.scale_f32) static_cast<float*>(sp)[so] = sc[it];
+        else static_cast<__half*>(sp)[so] = __float2half_rn(sc[it]);
+      }
+    }
+    return;
+  }
+  const bool bf = p.cache_dtype == PA_DTYPE_BF16;
 #pragma unroll
   for (int it = 0; it < C::NL; ++it) {
     const int j = it * C::RPI + sub;
     const int h = h0 + (j >> 1);
+    if (h >= p.Hkv) continue;
     const bool isv = j & 1;
-    const bool live = h < p.Hkv;
+    uint16_t* dst = static_cast<uint16_t*>(isv ? p.v : p.k) + (isv ? vb + h * p.v_shead : kb + h * p.k_shead) +
+                    part * EPL;
+    if constexpr (IN == PA_DTYPE_F16 || IN == PA_DTYPE_BF16) {
+      if ((IN == PA_DTYPE_BF16) == bf) {
+        *reinterpret_cast<uint4*>(dst) = raw[it];  // same 16-bit type: plain copy
+        continue;
+      }
+    }
     float f[EPL];
     unpack_row<IN, EPL>(raw[it], f);
-    const long long row = isv ? vb + h * p.v_shead : kb + h * p.k_shead;
-    if (p.cache_dtype == PA_DTYPE_I8) {
-      float amax = 0.f;
+    uint32_t w[EPL / 2];
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(f[i]));
-#pragma unroll
-      for (int o = C::LPR / 2; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const float sc = (amax == 0.f) ? 1.0f : __fdiv_rn(amax, 127.0f);
-      uint32_t w[EPL / 4];
-      const bool near = quant_row_fast<EPL>(f, rcp_approx(sc), w);
-      if (__any_sync(0xffffffffu, near)) quant_row_exact<EPL>(f, sc, w);
-      if (live) {
-        int8_t* dst = static_cast<int8_t*>(isv ? p.v : p.k) + row + part * EPL;
-        if constexpr (EPL == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-        else *reinterpret_cast<uint32_t*>(dst) = w[0];
-        if (part == 0) {
-          const long long so = isv ? vsb + h * p.vs_shead : ksb + h * p.ks_shead;
-          void* sp = isv ? p.vs : p.ks;
-          if (p.scale_f32) static_cast<float*>(sp)[so] = sc;
-          else static_cast<__half*>(sp)[so] = __float2half_rn(sc);
-        }
-      }
-    } else if (live) {
-      const bool bf = p.cache_dtype == PA_DTYPE_BF16;
-      uint16_t* dst = static_cast<uint16_t*>(isv ? p.v : p.k) + row + part * EPL;
-      if constexpr (IN == PA_DTYPE_F16 || IN == PA_DTYPE_BF16) {
-        if ((IN == PA_DTYPE_BF16) == bf) {
-          *reinterpret_cast<uint4*>(dst) = raw[it];  // same 16-bit type: plain copy
-          continue;
-        }
-      }
-      uint32_t w[EPL / 2];
-#pragma unroll
-      for (int i = 0; i < EPL / 2; ++i) w[i] = bf ? pack2<true>(f[2 * i], f[2 * i + 1]) : pack2<false>(f[2 * i], f[2 * i + 1]);
-      if constexpr (EPL == 8) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-    }
+    for (int i = 0; i < EPL / 2; ++i) w[i] = bf ? pack2<true>(f[2 * i], f[2 * i + 1]) : pack2<false>(f[2 * i], f[2 * i + 1]);
+    if constexpr (EPL == 8) *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
   }
 }
 
