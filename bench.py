@@ -128,75 +128,302 @@ class ClockSampler:
 # ----------------------------------------------------------------------------
 # workloads
 # ----------------------------------------------------------------------------
-def decode_workload(name: str, seed: int, device):
-    """Build the decode batch (on `device`) and the per-step call."""
-    from kernels.flash_attention import flash_attention_forward, write_kv_cache
-    from pie_b200.workloads import config_batch
+class Workload:
+    """One benchmark case: device step, end-to-end step, and a CPU-oracle sample.
 
-    b = config_batch(name, seed=seed)
-    g = b.to(device)
-    B, Hq, _, D = b.Q.shape
-    Hkv = b.K.shape[2]
-    sum_ctx = int(b.kv_len.long().sum())
-    kv_bytes = sum_ctx * Hkv * b.kv_bytes_per_token_head
-    qo_bytes = 2 * B * Hq * D * 2 + B * Hq * 2
-    info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": b.block_size, "sum_ctx": sum_ctx,
-            "kv_dtype": str(b.K.dtype).replace("torch.", "")}
-    write = None
-    if name == "decode_int8":
-        T_new = 64
-        gen = torch.Generator().manual_seed(seed + 99)
-        kn = (torch.randn(B * T_new, Hkv, D, generator=gen) *
-              torch.where(torch.rand(B * T_new, Hkv, D, generator=gen) < 0.01, 8.0, 1.0)).half().to(device)
-        vn = torch.randn(B * T_new, Hkv, D, generator=gen).half().to(device)
-        seq = torch.arange(B, dtype=torch.int32).repeat_interleave(T_new).to(device)
-        pos = (b.kv_len.view(-1, 1) - T_new + torch.arange(T_new).view(1, -1)).reshape(-1).to(torch.int32).to(device)
-        write = (kn, vn, seq, pos)
-        w_bytes = 2 * B * T_new * Hkv * (D * 2 + D + 2)
-        info["new_tokens_per_seq"] = T_new
-        kv_bytes += w_bytes
+    step()          one pass of the hot path over device-resident inputs
+    e2e_step()      the same through the public API with this step's inputs
+                    copied from pinned host memory and the result copied back
+    cpu_unit(i)     runs unit i of the reference's naive CPU path (the oracle
+                    restatement) and returns the work it did (bytes or FLOPs);
+                    units are small (tens of ms) so that samples stay bounded
+    """
 
-    def step(out=None):
-        if write is not None:
-            write_kv_cache(write[0], write[1], g.block_table, write[2], write[3], g.K, g.V, g.k_scale, g.v_scale)
-        return flash_attention_forward(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, g.block_size, g.kv_len,
-                                       g.k_scale, g.v_scale, out=out)
+    metric = unit = dtype = bound = kernel = ""
+    scale = 1.0
+    scaling = "weak"
+    launches = 1
+    h2d = d2h = 0
 
-    launches = 2 + (1 if write is not None else 0)
-    return b, g, step, kv_bytes + qo_bytes, info, launches
+    def cpu_sample(self, seconds: float, threads: int):
+        torch.set_num_threads(threads)
+        done, t, i = 0.0, 0.0, 0
+        while t < seconds or i == 0:
+            t0 = time.perf_counter()
+            done += self.cpu_unit(i)
+            t += time.perf_counter() - t0
+            i += 1
+        return t, done, i
 
 
-def prefill_workload(seed: int, device):
-    from kernels.flash_attention import flash_attention_forward, write_kv_cache
-    from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
+def _pin(*ts):
+    return [t.pin_memory() for t in ts]
 
-    cfg = CONFIGS["prefill_bf16"]
-    gen = torch.Generator().manual_seed(seed)
-    L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
-    B, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
-    bt, nblk, NB = block_tables(gen, L, BS)
-    maxL = max(L)
-    Q = torch.randn(B, Hq, maxL, D, generator=gen).to(torch.bfloat16)
-    T = sum(L)
-    kn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
-    vn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
-    seq = torch.cat([torch.full((l,), i, dtype=torch.int32) for i, l in enumerate(L)])
-    pos = torch.cat([torch.arange(l, dtype=torch.int32) for l in L])
-    d = lambda t: t.to(device)  # noqa: E731
-    Qd, knd, vnd, seqd, posd, btd, nbd = map(d, (Q, kn, vn, seq, pos, bt, nblk))
-    Ld = torch.tensor(L, dtype=torch.int32, device=device)
-    Kc = torch.empty(NB, BS, Hkv, D, dtype=torch.float16, device=device)
-    Vc = torch.empty_like(Kc)
 
-    def step(out=None):
-        write_kv_cache(knd, vnd, btd, seqd, posd, Kc, Vc)
-        return flash_attention_forward(Qd, Kc, Vc, Ld, btd, nbd, BS, Ld, None, None, out=out)
+class DecodeWorkload(Workload):
+    """decode_fp16 / decode_int8: B=64, 32/8 heads, D=128, ctx ~ U[512, 4096]."""
 
-    flops = sum(4.0 * Hq * D * l * (l + 1) / 2 for l in L)
-    info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS, "sum_len": T, "q_dtype": "bfloat16",
-            "kv_dtype": "float16"}
-    host = {"Q": Q, "kn": kn, "vn": vn, "seq": seq, "pos": pos, "bt": bt, "nblk": nblk, "L": torch.tensor(L)}
-    return host, step, flops, info
+    def __init__(self, name: str, seed: int, device, cpu_only: bool = False):
+        from pie_b200.workloads import config_batch
+
+        self.name = name
+        b = config_batch(name, seed=seed)
+        self.b = b
+        B, Hq, _, D = b.Q.shape
+        Hkv = b.K.shape[2]
+        self.sum_ctx = int(b.kv_len.long().sum())
+        kv_bytes = self.sum_ctx * Hkv * b.kv_bytes_per_token_head
+        qo_bytes = 2 * B * Hq * D * 2 + B * Hq * 2
+        self.info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": b.block_size, "sum_ctx": self.sum_ctx,
+                     "kv_dtype": str(b.K.dtype).replace("torch.", "")}
+        self.int8 = name == "decode_int8"
+        self.work = kv_bytes + qo_bytes
+        self.write = None
+        if self.int8:
+            T_new = 64
+            gen = torch.Generator().manual_seed(seed + 99)
+            kn = (torch.randn(B * T_new, Hkv, D, generator=gen) *
+                  torch.where(torch.rand(B * T_new, Hkv, D, generator=gen) < 0.01, 8.0, 1.0)).half()
+            vn = torch.randn(B * T_new, Hkv, D, generator=gen).half()
+            seq = torch.arange(B, dtype=torch.int32).repeat_interleave(T_new)
+            pos = (b.kv_len.view(-1, 1) - T_new + torch.arange(T_new).view(1, -1)).reshape(-1).to(torch.int32)
+            self.write = (kn, vn, seq, pos)
+            self.work += 2 * B * T_new * Hkv * (D * 2 + D + 2)
+            self.info["new_tokens_per_seq"] = T_new
+        self.unit, self.scale, self.bound, self.dtype = "GB/s", 1e-9, "hbm", "i8" if self.int8 else "f16"
+        self.metric = ("paged decode attention + quantise-on-write HBM GB/s (INT8 KV, B=64, 32/8 heads, D=128)"
+                       if self.int8 else
+                       "paged decode attention HBM GB/s (fp16 KV, B=64, 32/8 heads, D=128, ctx~U[512,4096])")
+        self.kernel = "paged_attn_decode (split + merge launches)" + (" + kv_write_quant" if self.int8 else "")
+        self.launches = 3 if self.int8 else 2
+        if not cpu_only:
+            self._device(device)
+
+    def _device(self, device):
+        from kernels.flash_attention import flash_attention_forward, write_kv_cache
+
+        b, g = self.b, self.b.to(device)
+        self.g = g
+        wd = None if self.write is None else [t.to(device) for t in self.write]
+
+        def step(out=None):
+            if wd is not None:
+                write_kv_cache(wd[0], wd[1], g.block_table, wd[2], wd[3], g.K, g.V, g.k_scale, g.v_scale)
+            return flash_attention_forward(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, g.block_size,
+                                           g.kv_len, g.k_scale, g.v_scale, out=out)
+        self.step = step
+
+        host = _pin(b.Q, b.block_table, b.num_blocks, b.q_len, b.kv_len, *(self.write or ()))
+        dev = [torch.empty_like(t, device=device) for t in host]
+        hO = torch.empty(b.Q.shape, dtype=torch.float16).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in host)
+        self.d2h = hO.numel() * hO.element_size()
+
+        def e2e_step():
+            for h, d in zip(host, dev):
+                d.copy_(h, non_blocking=True)
+            Q, bt, nb, ql, kl = dev[:5]
+            if self.write is not None:
+                write_kv_cache(dev[5], dev[6], bt, dev[7], dev[8], g.K, g.V, g.k_scale, g.v_scale)
+            O, _ = flash_attention_forward(Q, g.K, g.V, ql, bt, nb, g.block_size, kl, g.k_scale, g.v_scale)
+            hO.copy_(O, non_blocking=True)
+        self.e2e_step = e2e_step
+
+    def cpu_unit(self, i):
+        from oracle import paged_attention as orc
+
+        b = self.b
+        if not hasattr(self, "_np"):
+            self._np = (b.Q.float().numpy(), b.K.numpy(), b.V.numpy(),
+                        None if b.k_scale is None else b.k_scale.numpy(),
+                        None if b.v_scale is None else b.v_scale.numpy(),
+                        *[t.numpy() for t in (b.q_len, b.block_table, b.num_blocks, b.kv_len)])
+        Q, K, V, ks, vs, ql, bt, nb, kl = self._np
+        s = slice(i % len(kl), i % len(kl) + 1)
+        orc.paged_attention(Q[s], K, V, ql[s], bt[s], nb[s], b.block_size, kl[s], ks, vs)
+        return float(kl[s][0]) * K.shape[2] * b.kv_bytes_per_token_head
+
+    def sample_desc(self, n, t):
+        return f"{n} whole sequences of the workload, one at a time, {t:.1f} s"
+
+
+class PrefillWorkload(Workload):
+    """prefill_bf16: B=8, L ~ U[1024, 4096], 32/8 heads, D=128, bf16; write K/V then attend."""
+
+    ROWS = 64  # query rows per CPU unit
+
+    def __init__(self, seed: int, device, cpu_only: bool = False):
+        from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
+
+        cfg = CONFIGS["prefill_bf16"]
+        gen = torch.Generator().manual_seed(seed)
+        L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
+        B, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
+        bt, nblk, NB = block_tables(gen, L, BS)
+        maxL = max(L)
+        self.L, self.BS, self.NB = L, BS, NB
+        self.Q = torch.randn(B, Hq, maxL, D, generator=gen).to(torch.bfloat16)
+        T = sum(L)
+        self.kn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
+        self.vn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
+        self.seq = torch.cat([torch.full((l,), i, dtype=torch.int32) for i, l in enumerate(L)])
+        self.pos = torch.cat([torch.arange(l, dtype=torch.int32) for l in L])
+        self.bt, self.nblk = bt, nblk
+        self.Lt = torch.tensor(L, dtype=torch.int32)
+        self.work = sum(4.0 * Hq * D * l * (l + 1) / 2 for l in L)
+        self.info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS, "sum_len": T, "q_dtype": "bfloat16",
+                     "kv_dtype": "float16"}
+        self.unit, self.scale, self.bound, self.dtype = "TFLOP/s", 1e-12, "tensor", "bf16"
+        self.metric = "causal paged prefill TFLOP/s (bf16, B=8, L~U[1024,4096], 32/8 heads, D=128)"
+        self.kernel = "kv_write_copy + paged_attn_prefill"
+        self.launches = 2
+        self.Hq, self.D = Hq, D
+        if not cpu_only:
+            self._device(device)
+
+    def _device(self, device):
+        from kernels.flash_attention import flash_attention_forward, write_kv_cache
+
+        host = _pin(self.Q, self.kn, self.vn, self.seq, self.pos, self.bt, self.nblk, self.Lt)
+        dev = [t.to(device) for t in host]
+        Qd, knd, vnd, seqd, posd, btd, nbd, Ld = dev
+        Hkv, D = self.kn.shape[1], self.kn.shape[2]
+        Kc = torch.empty(self.NB, self.BS, Hkv, D, dtype=torch.float16, device=device)
+        Vc = torch.empty_like(Kc)
+
+        def step(out=None):
+            write_kv_cache(knd, vnd, btd, seqd, posd, Kc, Vc)
+            return flash_attention_forward(Qd, Kc, Vc, Ld, btd, nbd, self.BS, Ld, None, None, out=out)
+        self.step = step
+
+        ebuf = [torch.empty_like(t) for t in dev]
+        hO = torch.empty(self.Q.shape, dtype=torch.float16).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in host)
+        self.d2h = hO.numel() * hO.element_size()
+
+        def e2e_step():
+            for h, d in zip(host, ebuf):
+                d.copy_(h, non_blocking=True)
+            Q, kn, vn, seq, pos, bt, nb, Lx = ebuf
+            write_kv_cache(kn, vn, bt, seq, pos, Kc, Vc)
+            O, _ = flash_attention_forward(Q, Kc, Vc, Lx, bt, nb, self.BS, Lx, None, None)
+            hO.copy_(O, non_blocking=True)
+        self.e2e_step = e2e_step
+
+    def _cpu_pool(self):
+        # the copy-on-write of the new rows, done once (not timed)
+        import numpy as np
+
+        Hkv, D = self.kn.shape[1], self.kn.shape[2]
+        K = np.zeros((self.NB, self.BS, Hkv, D), np.float16)
+        V = np.zeros_like(K)
+        seq, pos, bt = self.seq.numpy(), self.pos.numpy(), self.bt.numpy()
+        blk = bt[seq, pos // self.BS]
+        K[blk, pos % self.BS] = self.kn.float().numpy().astype(np.float16)
+        V[blk, pos % self.BS] = self.vn.float().numpy().astype(np.float16)
+        units = [(b, lo) for b, l in enumerate(self.L) for lo in range(0, l, self.ROWS)]
+        order = np.random.default_rng(0).permutation(len(units))
+        return K, V, [units[j] for j in order]
+
+    def cpu_unit(self, i):
+        """Query rows [lo, lo + ROWS) of one sequence against its causal keys."""
+        from oracle import paged_attention as orc
+
+        if not hasattr(self, "_cpu"):
+            self._cpu = self._cpu_pool()
+        K, V, units = self._cpu
+        b, lo = units[i % len(units)]
+        l = self.L[b]
+        hi = min(l, lo + self.ROWS)
+        q = self.Q[b:b + 1, :, lo:hi].float().numpy()
+        # bottom-right causal with kv_len = hi: row m (absolute lo + m) sees keys 0..lo+m
+        orc.paged_attention(q, K, V, [hi - lo], self.bt[b:b + 1].numpy(), self.nblk[b:b + 1].numpy(), self.BS, [hi])
+        return 4.0 * self.Hq * self.D * sum(r + 1 for r in range(lo, hi))
+
+    def sample_desc(self, n, t):
+        return f"{n} blocks of {self.ROWS} query rows drawn from the workload's sequences, {t:.1f} s"
+
+
+class LongCtxWorkload(Workload):
+    """long_ctx_int8: B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8; KV heads sharded over ranks."""
+
+    def __init__(self, ws: int, rank: int, device, cpu_only: bool = False):
+        from pie_b200.workloads import CONFIGS, draw_context_lengths
+
+        cfg = CONFIGS["long_ctx_int8"]
+        self.cfg = cfg
+        Bn, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
+        gen = torch.Generator().manual_seed(0)
+        self.ctx = draw_context_lengths(gen, Bn, *cfg["ctx_range"])  # same sequences on every rank
+        self.sum_ctx = sum(self.ctx)
+        self.work = self.sum_ctx * Hkv * (2 * D + 4) + 2 * Bn * Hq * D * 2
+        self.info = {"B": Bn, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS, "sum_ctx": self.sum_ctx}
+        self.unit, self.scale, self.bound, self.dtype = "GB/s", 1e-9, "hbm", "i8"
+        self.scaling = "strong"
+        self.metric = ("long-context paged decode HBM GB/s, KV heads sharded over GPUs (INT8 KV, B=256, 64/8 heads, "
+                       "ctx~U[8192,32768])")
+        self.kernel = "paged_attn_decode per GPU (split + merge, + NCCL all_gather)"
+        self.launches = 2
+        self.ws, self.rank = ws, rank
+        if not cpu_only:
+            self._device(device)
+
+    def _device(self, device):
+        from pie_b200.sharded import KVHeadShardedDecoder, build_rank_pool
+
+        c = self.cfg
+        Bn, Hq, Hkv, D, BS = c["B"], c["Hq"], c["Hkv"], c["D"], c["BS"]
+        dec = KVHeadShardedDecoder(Hq, Hkv, D)
+        K, V, ks, vs, bt, nblk, NB = build_rank_pool(self.ctx, Hkv // self.ws, D, BS, 1000 + self.rank, device)
+        Qfull = torch.randn(Bn, Hq, 1, D, generator=torch.Generator().manual_seed(5)).half()
+        Ql = dec.local_q(Qfull).contiguous().to(device)
+        ql = torch.ones(Bn, dtype=torch.int32, device=device)
+        kl = torch.tensor(self.ctx, dtype=torch.int32, device=device)
+
+        def step():
+            return dec.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs)
+        self.step = step
+
+        host = _pin(dec.local_q(Qfull).contiguous(), bt.cpu(), nblk.cpu(), ql.cpu(), kl.cpu())
+        dev = [torch.empty_like(t, device=device) for t in host]
+        hO = torch.empty(Bn, Hq, 1, D, dtype=torch.float16).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in host)
+        self.d2h = hO.numel() * hO.element_size()
+
+        def e2e_step():
+            for h, d in zip(host, dev):
+                d.copy_(h, non_blocking=True)
+            O = dec.forward(dev[0], K, V, dev[3], dev[1], dev[2], BS, dev[4], ks, vs)
+            hO.copy_(O, non_blocking=True)
+        self.e2e_step = e2e_step
+
+    def cpu_unit(self, i):
+        """One sequence of the workload's shape (ctx from its range) over all 8 KV heads."""
+        from oracle import paged_attention as orc
+        from pie_b200.workloads import make_decode_batch
+
+        if not hasattr(self, "_cpu"):
+            c = self.cfg
+            ctx = self.ctx[:4]
+            b = make_decode_batch(1000, len(ctx), c["Hq"], c["Hkv"], c["D"], c["BS"], ctx, kv_dtype=torch.int8,
+                                  outliers=0.01)
+            self._cpu = (b, b.Q.float().numpy(), b.K.numpy(), b.V.numpy(), b.k_scale.numpy(), b.v_scale.numpy(),
+                         *[t.numpy() for t in (b.q_len, b.block_table, b.num_blocks, b.kv_len)])
+        b, Q, K, V, ks, vs, ql, bt, nb, kl = self._cpu
+        s = slice(i % len(kl), i % len(kl) + 1)
+        orc.paged_attention(Q[s], K, V, ql[s], bt[s], nb[s], b.block_size, kl[s], ks, vs)
+        return float(kl[s][0]) * K.shape[2] * b.kv_bytes_per_token_head
+
+    def sample_desc(self, n, t):
+        return f"{n} sequences (4 distinct, ctx from the workload's range, all 8 KV heads), {t:.1f} s"
+
+
+def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False) -> Workload:
+    if name == "prefill_bf16":
+        return PrefillWorkload(1000 + rank, device, cpu_only)
+    if name == "long_ctx_int8":
+        return LongCtxWorkload(ws, rank, device, cpu_only)
+    return DecodeWorkload(name, 1000 + rank, device, cpu_only)
 
 
 # ----------------------------------------------------------------------------
@@ -239,31 +466,6 @@ def read_traffic(name: str):
     return None
 
 
-def cpu_baseline_decode(b, seconds: float, threads: int):
-    """The reference's naive paged attention (oracle restatement) on the host CPU."""
-    from oracle import paged_attention as orc
-
-    torch.set_num_threads(threads)
-    Qn = b.Q.float().numpy()
-    Kn, Vn = b.K.numpy(), b.V.numpy()
-    ks = None if b.k_scale is None else b.k_scale.numpy()
-    vs = None if b.v_scale is None else b.v_scale.numpy()
-    meta = [t.numpy() for t in (b.q_len, b.block_table, b.num_blocks, b.kv_len)]
-    B = Qn.shape[0]
-    times, seqs_done, t_end = [], 0, time.perf_counter() + seconds
-    i = 0
-    while time.perf_counter() < t_end or not times:
-        sl = slice(i % B, i % B + 1)
-        t0 = time.perf_counter()
-        orc.paged_attention(Qn[sl], Kn, Vn, meta[0][sl], meta[1][sl], meta[2][sl], b.block_size, meta[3][sl], ks, vs)
-        times.append((time.perf_counter() - t0, int(meta[3][sl][0])))
-        seqs_done += 1
-        i += 1
-    t = sum(x[0] for x in times)
-    ctx = sum(x[1] for x in times)
-    return t, ctx, seqs_done
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -280,66 +482,53 @@ def main():
     ws, rank, local = dist_env()
     if a.impl == "reference":
         return run_reference(a, ws, rank)
-    if a.workload == "long_ctx_int8":
-        from pie_b200.sharded import bench_long_ctx
-        return bench_long_ctx(a, ws, rank, local)
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if ws > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=device)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     peaks, peak_kind = load_peaks()
-    seed = 1000 + rank
-
-    if a.workload == "prefill_bf16":
-        host, step, work, info, launches = *prefill_workload(seed, device), 2
-        unit, metric = "TFLOP/s", "causal paged prefill TFLOP/s (bf16, B=8, L~U[1024,4096], 32/8 heads, D=128)"
-        scale = 1e-12
-        bound, peak, punit = "tensor", peaks["bf16_tflops"], "TFLOP/s"
+    w = make_workload(a.workload, ws, rank, device)
+    if w.bound == "hbm":
+        peak, punit = peaks["hbm_gbs"], "GB/s"
     else:
-        b, g, step, work, info, launches = decode_workload(a.workload, seed, device)
-        unit = "GB/s"
-        metric = ("paged decode attention HBM GB/s (fp16 KV, B=64, 32/8 heads, D=128, ctx~U[512,4096])"
-                  if a.workload == "decode_fp16" else
-                  "paged decode attention + quantise-on-write HBM GB/s (INT8 KV, B=64, 32/8 heads, D=128)")
-        scale = 1e-9
-        bound, peak, punit = "hbm", peaks["hbm_gbs"], "GB/s"
+        peak, punit = peaks["bf16_tflops"], "TFLOP/s"
 
     with ClockSampler(local) as clk:
-        ms = time_steps(step, a.steps, a.warmup, device, ws)
+        ms = time_steps(w.step, a.steps, a.warmup, device, ws)
     ms_step = ms / a.steps
-    value = ws * work / (ms_step * 1e-3) * scale
+    # weak scaling: every rank runs its own batch; strong: the ranks share one
+    total_work = w.work * (ws if w.scaling == "weak" else 1)
+    value = total_work / (ms_step * 1e-3) * w.scale
+    per_gpu = value / ws
 
-    # e2e: host buffers in, result back to host, through the public API
-    e2e = e2e_measure(a, step, device, ws, (b if a.workload != "prefill_bf16" else None),
-                      (g if a.workload != "prefill_bf16" else None), work, scale)
+    e2e_steps = max(10, a.steps // 10)
+    e_ms = time_steps(w.e2e_step, e2e_steps, a.warmup, device, ws) / e2e_steps
+    e2e = {"value": round(total_work / (e_ms * 1e-3) * w.scale, 2), "unit": w.unit, "h2d_bytes_per_step": w.h2d,
+           "d2h_bytes_per_step": w.d2h, "steps": e2e_steps, "ms_per_step": round(e_ms, 5)}
 
-    achieved = work / (ms_step * 1e-3) * scale
-    traffic = read_traffic(f"{a.workload}_dominant_kernel")
     line = {
-        "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": ws, "steps": a.steps,
+        "metric": w.metric, "value": round(value, 2), "unit": w.unit, "n_gpus": ws, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "us_per_step": round(ms_step * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f16" if a.workload == "decode_fp16" else ("i8" if a.workload == "decode_int8" else "bf16"),
+        "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
-        "config": {"workload": a.workload, **info, "parallelism": f"dp{ws} (one batch per rank)",
+        "config": {"workload": a.workload, **w.info,
+                   "parallelism": (f"kv-head shard x{ws} + NCCL all_gather" if w.scaling == "strong"
+                                   else f"dp{ws} (one batch per rank)"),
                    "l2": "inputs larger than L2 (126 MB)"},
-        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": punit,
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "paged_attn_decode (split + merge launches)" if bound == "hbm" else
-                               "kv_write_copy + paged_attn_prefill", "peak_source": f"{peak_kind} MEASURED_PEAKS"},
+        "roofline": {"bound": w.bound, "achieved": round(per_gpu, 2), "peak": peak, "unit": punit,
+                     "frac": round(per_gpu / peak, 4), "traffic": read_traffic(f"{a.workload}_dominant_kernel"),
+                     "kernel": w.kernel, "peak_source": f"{peak_kind} MEASURED_PEAKS"},
         "e2e": e2e,
-        "gpu_launches": launches * a.steps,
+        "gpu_launches": w.launches * a.steps,
         "clocks": clk.summary(),
     }
-    if rank == 0 and ws == 1 and not a.no_cpu_baseline and a.workload != "prefill_bf16":
+    if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        t, ctx, nseq = cpu_baseline_decode(b, a.cpu_seconds, threads)
-        kvb = ctx * info["Hkv"] * b.kv_bytes_per_token_head
-        line["cpu_baseline"] = {"value": round(kvb / t * 1e-9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                                "sample": f"{nseq} sequences of the workload, one at a time, {t:.1f} s"}
+        t, done, n = w.cpu_sample(a.cpu_seconds, threads)
+        line["cpu_baseline"] = {"value": round(done / t * w.scale, 4), "unit": w.unit, "cores": threads,
+                                "kind": "port", "sample": w.sample_desc(n, t)}
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -347,71 +536,35 @@ def main():
         print(json.dumps(line))
 
 
-def e2e_measure(a, step, device, ws, b, g, work, scale):
-    """Same metric through the public API with host-resident step inputs.
-
-    Per step: pinned host -> device copy of the step's inputs (Q and the paging
-    metadata; the KV pool is device-resident state), the call, and the
-    device -> host copy of O.  Timed with CUDA events like the device number.
-    """
-    if b is None:
-        return None
-    from kernels.flash_attention import flash_attention_forward
-
-    hQ = b.Q.pin_memory()
-    hbt, hnb, hql, hkl = (t.pin_memory() for t in (b.block_table, b.num_blocks, b.q_len, b.kv_len))
-    hO = torch.empty(b.Q.shape, dtype=torch.float16).pin_memory()
-    dQ = torch.empty_like(g.Q)
-    dbt, dnb, dql, dkl = (torch.empty_like(t) for t in (g.block_table, g.num_blocks, g.q_len, g.kv_len))
-    h2d = sum(t.numel() * t.element_size() for t in (hQ, hbt, hnb, hql, hkl))
-    d2h = hO.numel() * hO.element_size()
-
-    def e2e_step():
-        for h, d in ((hQ, dQ), (hbt, dbt), (hnb, dnb), (hql, dql), (hkl, dkl)):
-            d.copy_(h, non_blocking=True)
-        O, _ = flash_attention_forward(dQ, g.K, g.V, dql, dbt, dnb, g.block_size, dkl, g.k_scale, g.v_scale)
-        hO.copy_(O, non_blocking=True)
-
-    steps = max(10, a.steps // 10)
-    ms = time_steps(e2e_step, steps, a.warmup, device, ws)
-    val = ws * work / (ms / steps * 1e-3) * scale
-    return {"value": round(val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "ms_per_step": round(ms / steps, 5)}
-
-
 def run_reference(a, ws, rank):
-    """Reference arm: the reference's CPU path (naive PyTorch paged attention) on the host."""
+    """Reference arm: the reference's own path for this hot path on the host CPU.
+
+    The reference's naive PyTorch paged attention (restated in oracle/; the
+    reference's Triton kernel needs a GPU build of the reference) runs on all
+    host threads, one bounded sample of the workload per step.  Under torchrun
+    only rank 0 runs it.
+    """
     if rank != 0:
         return
-    from pie_b200.workloads import config_batch
-
     threads = os.cpu_count() or 1
-    if a.workload in ("decode_fp16", "decode_int8"):
-        b = config_batch(a.workload, seed=1000)
-        ms_list, bytes_list = [], []
-        for _ in range(a.warmup):
-            cpu_baseline_decode(b, 0.0, threads)
-        for _ in range(a.steps):
-            t, ctx, n = cpu_baseline_decode(b, min(2.0, 120.0 / max(1, a.steps)), threads)
-            ms_list.append(t)
-            bytes_list.append(ctx * b.K.shape[2] * b.kv_bytes_per_token_head)
-        t = sum(ms_list)
-        val = sum(bytes_list) / t * 1e-9
-        unit = "GB/s"
-        metric = ("paged decode attention HBM GB/s (fp16 KV, B=64, 32/8 heads, D=128, ctx~U[512,4096])"
-                  if a.workload == "decode_fp16" else
-                  "paged decode attention + quantise-on-write HBM GB/s (INT8 KV, B=64, 32/8 heads, D=128)")
-        sample = f"{a.steps} samples of whole sequences of the workload, {t:.1f} s total"
-    else:
-        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU arm covers decode workloads only"}))
-        return
-    line = {"impl": "reference", "metric": metric, "value": round(val, 4), "unit": unit, "n_gpus": ws,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t / a.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+    w = make_workload(a.workload, ws, rank, None, cpu_only=True)
+    budget = min(2.0, 120.0 / max(1, a.steps + a.warmup))
+    for _ in range(a.warmup):
+        w.cpu_sample(0.0, threads)
+    t_tot, done_tot, n_tot = 0.0, 0.0, 0
+    for _ in range(a.steps):
+        t, done, n = w.cpu_sample(budget, threads)
+        t_tot, done_tot, n_tot = t_tot + t, done_tot + done, n_tot + n
+    val = done_tot / t_tot * w.scale
+    sample = f"{a.steps} steps of {budget * 1e3:.0f} ms: " + w.sample_desc(n_tot, t_tot)
+    line = {"impl": "reference", "metric": w.metric, "value": round(val, 4), "unit": w.unit, "n_gpus": ws,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_tot / a.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
-            "config": {"workload": a.workload, "threads": threads},
-            "cpu_baseline": {"value": round(val, 4), "unit": unit, "cores": threads, "kind": "port", "sample": sample},
-            "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": {"workload": a.workload, **w.info, "threads": threads},
+            "cpu_baseline": {"value": round(val, 4), "unit": w.unit, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(val, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 

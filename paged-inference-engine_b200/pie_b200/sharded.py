@@ -12,10 +12,6 @@ the paged-attention hot path (kernels/flash_attention.py:139-172 per rank).
 """
 from __future__ import annotations
 
-import json
-import math
-import os
-import time
 from typing import Callable, Optional
 
 import torch
@@ -102,60 +98,3 @@ def build_rank_pool(ctx: list[int], Hkv_local: int, D: int, BS: int, seed: int, 
             pool[lo:hi] = q
             sc[lo:hi] = s
     return K, V, ks, vs, bt.to(device), nblk.to(device), NB
-
-
-def bench_long_ctx(a, ws: int, rank: int, local: int) -> None:
-    """bench.py --workload long_ctx_int8: B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8."""
-    import datetime
-
-    import bench as B_
-    from .workloads import CONFIGS, draw_context_lengths
-
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if ws > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    cfg = CONFIGS["long_ctx_int8"]
-    Bn, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
-    gen = torch.Generator().manual_seed(0)
-    ctx = draw_context_lengths(gen, Bn, *cfg["ctx_range"])  # same sequences on every rank
-    dec = KVHeadShardedDecoder(Hq, Hkv, D)
-    hkv_loc = Hkv // ws
-    K, V, ks, vs, bt, nblk, NB = build_rank_pool(ctx, hkv_loc, D, BS, 1000 + rank, device)
-    Qfull = torch.randn(Bn, Hq, 1, D, generator=torch.Generator().manual_seed(5)).half().to(device)
-    Ql = dec.local_q(Qfull).contiguous()
-    ql = torch.ones(Bn, dtype=torch.int32, device=device)
-    kl = torch.tensor(ctx, dtype=torch.int32, device=device)
-
-    def step():
-        return dec.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs)
-
-    sum_ctx = sum(ctx)
-    total_bytes = sum_ctx * Hkv * (2 * D + 4) + 2 * Bn * Hq * D * 2
-    peaks, peak_kind = B_.load_peaks()
-    with B_.ClockSampler(local) as clk:
-        ms = B_.time_steps(step, a.steps, a.warmup, device, ws)
-    ms_step = ms / a.steps
-    value = total_bytes / (ms_step * 1e-3) * 1e-9
-    per_gpu = value / ws
-    line = {
-        "metric": "long-context paged decode HBM GB/s, KV heads sharded over GPUs (INT8 KV, B=256, 64/8 heads, "
-                  "ctx~U[8192,32768])",
-        "value": round(value, 2), "unit": "GB/s", "n_gpus": ws, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(ms_step, 5), "us_per_step": round(ms_step * 1e3, 2), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "i8",
-        "data": "synthetic (seeded N(0,1) with 1% outliers x8, quantised per token)",
-        "config": {"workload": "long_ctx_int8", "B": Bn, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS,
-                   "sum_ctx": sum_ctx, "parallelism": f"kv-head shard x{ws} + NCCL all_gather",
-                   "l2": "inputs larger than L2 (126 MB)"},
-        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(per_gpu / peaks["hbm_gbs"], 4), "traffic": None,
-                     "kernel": "paged_attn_decode per GPU (+ all_gather)", "peak_source": f"{peak_kind} MEASURED_PEAKS"},
-        "gpu_launches": 2 * a.steps,
-        "clocks": clk.summary(),
-    }
-    if ws > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line))
