@@ -161,7 +161,7 @@ __device__ __forceinline__ void set_status(int* status, int bit) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + TMA (cp.async.bulk.tensor, never with .multicast::cluster).
+// mbarrier + TMA (cp.async.bulk.tensor, single-CTA destination only).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
