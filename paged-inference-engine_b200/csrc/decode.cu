@@ -302,6 +302,7 @@ __device__ __forceinline__ float scale_from_word(uint32_t w, bool hi, int is_f32
 template <int D, int KVT, int QT, int NT, bool TMA>
 __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
     pa_decode_kernel(const AttnParams p, const __grid_constant__ KvMaps maps) {
+  pdl_enter();
   using C = DecCfg<D, KVT>;
   using Lay = DecLayout<D, KVT, NT>;
   constexpr int STAGES = C::STAGES;
@@ -882,6 +883,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
 // grid (Hkv, B), 128 threads.
 template <int D>
 __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p) {
+  pdl_enter();
   const int kvh = blockIdx.x;
   const int b = blockIdx.y;
   const int qlen = seq_qlen(p, b);
@@ -973,10 +975,12 @@ struct DecodeInst {
     auto kern = pa_decode_kernel<D, KVT, QT, NT, TMA>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
     if (e != cudaSuccess) return e;
-    kern<<<pl.ctas, pl.warps_per_cta * 32, pl.smem, stream>>>(p, maps);
+    e = launch_pdl(kern, dim3(pl.ctas), dim3(pl.warps_per_cta * 32), pl.smem, stream, p, maps);
+    if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    pa_decode_merge_kernel<D><<<dim3(p.Hkv, p.B), 128, 0, stream>>>(p);
+    e = launch_pdl(pa_decode_merge_kernel<D>, dim3(p.Hkv, p.B), dim3(128), 0, stream, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   }
 };

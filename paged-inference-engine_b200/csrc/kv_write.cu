@@ -121,6 +121,7 @@ __device__ __noinline__ void quant_row_exact(const float (&f)[EPL], float s, uin
 // block-table entry is known, so the index lookups overlap the row loads.
 template <int IN, int D>
 __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
+  pdl_enter();
   using C = WCfg<IN, D>;
   constexpr int EPL = C::EPL;
   const int lane = threadIdx.x & 31;
@@ -252,8 +253,7 @@ cudaError_t launch_in(const WriteParams& p, cudaStream_t stream) {
   auto go = [&](auto kern, int hg) {
     const long long warps = static_cast<long long>(p.T) * ((p.Hkv + hg - 1) / hg);
     const long long blocks = (warps * 32 + 255) / 256;
-    kern<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
   };
   if (p.D == 64) return go(kv_write_kernel<IN, 64>, WCfg<IN, 64>::HG);
   if (p.D == 128) return go(kv_write_kernel<IN, 128>, WCfg<IN, 128>::HG);

@@ -9,8 +9,38 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <utility>
 
 #include "pa_types.h"
+
+namespace pa {
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialisation (launch_pdl) and starts with
+// pdl_enter(): it waits until the previous grid in the stream has completed
+// and its writes are visible (so no input is read early), then lets the next
+// grid be scheduled.  The next grid's CTAs become resident while this one
+// runs and start as soon as it finishes, instead of after a launch gap.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+}  // namespace pa
 
 namespace pa {
 

@@ -156,6 +156,7 @@ __device__ __forceinline__ void pf_convert(const unsigned char* st, unsigned cha
 
 template <int D, int KVT, int QT>
 __global__ void __launch_bounds__(PF_THREADS) pa_prefill_kernel(const AttnParams p) {
+  pdl_enter();
   using C = PfCfg<D, KVT>;
   constexpr bool INT8 = C::INT8;
   constexpr bool MB = (KVT == KV_BF16);
@@ -380,7 +381,8 @@ cudaError_t pf_launch(const AttnParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const dim3 grid((p.maxq + PF_BM - 1) / PF_BM, p.Hq, p.B);
-  kern<<<grid, PF_THREADS, C::SMEM, stream>>>(p);
+  const cudaError_t le = launch_pdl(kern, grid, dim3(PF_THREADS), C::SMEM, stream, p);
+  if (le != cudaSuccess) return le;
   return cudaGetLastError();
 }
 

@@ -100,6 +100,7 @@ __device__ __noinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uin
 template <bool MMA_BF16, bool Q_CONVERT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     pa_prefill_tc_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
+  pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int mtile = gridDim.x - 1 - blockIdx.x;  // longest (causal) tiles first
   const int hq = blockIdx.y;
@@ -396,6 +397,7 @@ enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, 
 template <bool MMA_BF16, bool Q_CONVERT>
 __global__ void __launch_bounds__(P2_THREADS, 1)
     pa_prefill_tc2_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
+  pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int mtile = gridDim.x - 1 - blockIdx.x;
   const int pairs = p.G >> 1;
@@ -763,7 +765,8 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
     auto launch2 = [&](auto kern) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM);
       if (e != cudaSuccess) return e;
-      kern<<<grid2, P2_THREADS, P2_SMEM, stream>>>(p, maps);
+      e = launch_pdl(kern, grid2, dim3(P2_THREADS), P2_SMEM, stream, p, maps);
+      if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
     if (mma_bf16) return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
@@ -773,7 +776,8 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
   auto launch = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     if (e != cudaSuccess) return e;
-    kern<<<grid, TC_THREADS, TC_SMEM, stream>>>(p, maps);
+    e = launch_pdl(kern, grid, dim3(TC_THREADS), TC_SMEM, stream, p, maps);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };
   if (mma_bf16) return convert ? launch(pa_prefill_tc_kernel<true, true>) : launch(pa_prefill_tc_kernel<true, false>);
