@@ -11,7 +11,7 @@
 //   q_d    = clamp(round_half_even(x_d / scale), -127, 127)
 //                                     (tests/pre_quantize_test.py:11,
 //                                      transformer/model.py:105-114)
-// scale is the correctly rounded __fdiv_rn, and each q_d equals
+// scale is the correctly rounded quotient (div127_rn), and each q_d equals
 // __float2int_rn(__fdiv_rn(x_d, scale)) (quant_row_fast below), so the int8
 // values are bit-identical to torch's round(x / scale).clamp(-127, 127) on the
 // same fp32 inputs.  The stored scale is `scale` rounded to the pool's scale
@@ -20,6 +20,9 @@
 
 #ifndef PA_WRITE_NL
 #define PA_WRITE_NL 4
+#endif
+#ifndef PA_WRITE_MINB
+#define PA_WRITE_MINB 4
 #endif
 
 namespace pa {
@@ -72,6 +75,20 @@ __device__ __forceinline__ void unpack_row(const uint4& w, float (&f)[EPL]) {
 // |x| <= absmax gives |fl(x / s)| <= 127 * (1 + 2^-23) and
 // |y| <= 127 * (1 + 2^-21), both rounding to at most 127 in magnitude.
 constexpr float RNE_MAGIC = 12582912.0f;  // 1.5 * 2^23
+
+// RN(a / 127) without a division: y = RN(a * c) with c = RN(1 / 127), then
+// one FMA correction -- the multiply-and-correct scheme for a divisor known
+// in advance (Brisebarre, Muller, Raina, "Accelerating correctly rounded
+// floating-point division when the divisor is known in advance", IEEE Trans.
+// Computers 53(8), 2004).  For the divisor 127 it returns the correctly
+// rounded quotient for every non-negative finite float (checked exhaustively
+// against IEEE division; tests/test_div127_cpu.py restates the check).
+__device__ __forceinline__ float div127_rn(float a) {
+  constexpr float c = 1.0f / 127.0f;
+  const float y = __fmul_rn(a, c);
+  const float r = __fmaf_rn(-y, 127.0f, a);
+  return __fmaf_rn(r, c, y);
+}
 constexpr float NEAR_HALF = 0.5f - 1.0e-4f;
 
 __device__ __forceinline__ uint32_t q_byte(float y) { return __float_as_uint(y + RNE_MAGIC); }
@@ -106,7 +123,7 @@ __device__ __forceinline__ bool quant_row_fast(const float (&f)[EPL], float inv,
 }
 
 template <int EPL>
-__device__ __noinline__ void quant_row_exact(const float (&f)[EPL], float s, uint32_t (&w)[EPL / 4]) {
+__device__ __forceinline__ void quant_row_exact(const float (&f)[EPL], float s, uint32_t (&w)[EPL / 4]) {
 #pragma unroll
   for (int i = 0; i < EPL / 4; ++i) {
     uint32_t b[4];
@@ -120,7 +137,7 @@ __device__ __noinline__ void quant_row_exact(const float (&f)[EPL], float s, uin
 // heads): the group's K and V source rows are loaded before the token's
 // block-table entry is known, so the index lookups overlap the row loads.
 template <int IN, int D>
-__global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
+__global__ void __launch_bounds__(256, PA_WRITE_MINB) kv_write_kernel(const WriteParams p) {
   pdl_enter();
   using C = WCfg<IN, D>;
   constexpr int EPL = C::EPL;
@@ -173,13 +190,13 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
   // before the next, so their latencies overlap.
   if (p.cache_dtype == PA_DTYPE_I8) {
     float am[C::NL];
+    float fv[C::NL][EPL];
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
-      float f[EPL];
-      unpack_row<IN, EPL>(raw[it], f);
+      unpack_row<IN, EPL>(raw[it], fv[it]);
       float a = 0.f;
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) a = fmaxf(a, fabsf(f[i]));
+      for (int i = 0; i < EPL; ++i) a = fmaxf(a, fabsf(fv[it][i]));
       am[it] = a;
     }
 #pragma unroll
@@ -191,19 +208,13 @@ __global__ void __launch_bounds__(256) kv_write_kernel(const WriteParams p) {
     unsigned near = 0;
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
-      sc[it] = (am[it] == 0.f) ? 1.0f : __fdiv_rn(am[it], 127.0f);
-      float f[EPL];
-      unpack_row<IN, EPL>(raw[it], f);
-      if (quant_row_fast<EPL>(f, rcp_approx(sc[it]), w[it])) near |= 1u << it;
+      sc[it] = (am[it] == 0.f) ? 1.0f : div127_rn(am[it]);
+      if (quant_row_fast<EPL>(fv[it], rcp_approx(sc[it]), w[it])) near |= 1u << it;
     }
     // rows with a quotient near a rounding boundary: redo with the division
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
-      if (__any_sync(0xffffffffu, (near >> it) & 1u)) {
-        float f[EPL];
-        unpack_row<IN, EPL>(raw[it], f);
-        quant_row_exact<EPL>(f, sc[it], w[it]);
-      }
+      if (__any_sync(0xffffffffu, (near >> it) & 1u)) quant_row_exact<EPL>(fv[it], sc[it], w[it]);
     }
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
