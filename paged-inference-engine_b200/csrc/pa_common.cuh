@@ -280,6 +280,74 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// The 8 K16 steps of a head_dim-128 contraction in one block, D (tmem) =
+// sum_k A_k B_k with both operands K-major SW128 in shared memory: A_k and B_k
+// are the descriptors a0 / b0 advanced by 32 bytes per step within a 64-column
+// half and by AH / BH (16-byte units) from the first half to the second.  One
+// descriptor pair is computed by the caller; the rest are immediate adds.
+template <int AH, int BH>
+__device__ __forceinline__ void tc_mma_ss_k128(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p0, p1;\n .reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n"
+      " setp.ne.b32 p0, %3, %3;\n setp.eq.b32 p1, %3, %3;\n"
+      " add.s64 a1, %1, 2;\n add.s64 a2, %1, 4;\n add.s64 a3, %1, 6;\n"
+      " add.s64 a4, %1, %4;\n add.s64 a5, a4, 2;\n add.s64 a6, a4, 4;\n add.s64 a7, a4, 6;\n"
+      " add.s64 b1, %2, 2;\n add.s64 b2, %2, 4;\n add.s64 b3, %2, 6;\n"
+      " add.s64 b4, %2, %5;\n add.s64 b5, b4, 2;\n add.s64 b6, b4, 4;\n add.s64 b7, b4, 6;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n}\n" ::"r"(d_tmem),
+      "l"(a0), "l"(b0), "r"(idesc), "n"(AH), "n"(BH)
+      : "memory");
+}
+
+// NK K16 steps (NK = 4 or 8) with A in TMEM (8 columns of packed 16-bit
+// values per step) and B an MN-major SW128 descriptor advanced by 16 rows of
+// 128 bytes per step: D (tmem) (+)= sum_k A_k B_k; the first step accumulates
+// onto D only when `accumulate` is non-zero.
+template <int NK>
+__device__ __forceinline__ void tc_mma_ts_seq(uint32_t d_tmem, uint32_t a_tmem, uint64_t b0, uint32_t idesc,
+                                              uint32_t accumulate) {
+  static_assert(NK == 4 || NK == 8, "4 or 8 steps");
+  if constexpr (NK == 4) {
+    asm volatile(
+        "{\n .reg .pred p0, p1;\n .reg .b32 t1, t2, t3;\n .reg .b64 b1, b2, b3;\n"
+        " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %3, %3;\n"
+        " add.u32 t1, %1, 8;\n add.u32 t2, %1, 16;\n add.u32 t3, %1, 24;\n"
+        " add.s64 b1, %2, 128;\n add.s64 b2, %2, 256;\n add.s64 b3, %2, 384;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, p1;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p0, p1;\n .reg .b32 t1, t2, t3, t4, t5, t6, t7;\n"
+        " .reg .b64 b1, b2, b3, b4, b5, b6, b7;\n"
+        " setp.ne.b32 p0, %4, 0;\n setp.eq.b32 p1, %3, %3;\n"
+        " add.u32 t1, %1, 8;\n add.u32 t2, %1, 16;\n add.u32 t3, %1, 24;\n add.u32 t4, %1, 32;\n"
+        " add.u32 t5, %1, 40;\n add.u32 t6, %1, 48;\n add.u32 t7, %1, 56;\n"
+        " add.s64 b1, %2, 128;\n add.s64 b2, %2, 256;\n add.s64 b3, %2, 384;\n add.s64 b4, %2, 512;\n"
+        " add.s64 b5, %2, 640;\n add.s64 b6, %2, 768;\n add.s64 b7, %2, 896;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t1], b1, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t2], b2, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t3], b3, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t4], b4, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t5], b5, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t6], b6, %3, p1;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [t7], b7, %3, p1;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b0), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
 // 32 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(

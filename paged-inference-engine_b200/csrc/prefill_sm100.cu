@@ -2,28 +2,31 @@
 //
 // Replaces the q_len > 1 use of flash_attention_kernel
 // (kernels/flash_attention.py:19-136) for 16-bit pools with head_dim 128.
-// One CTA computes 128 query rows of one query head (FlashAttention-2
-// recurrence, kernels/flash_attention.py:102-123), with warp-specialised roles:
+// A CTA computes 128 query rows (FlashAttention-2 recurrence,
+// kernels/flash_attention.py:102-123) with warp-specialised roles:
 //
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 128 keys
-//               gathered through the block table (one 4-D TMA box per block and
-//               per 64 columns of head_dim) into a two-stage ring.  Boxes past
-//               the sequence or of an out-of-pool block id are fetched at an
-//               out-of-range block coordinate, which TMA fills with zeros.
-//   warp 5      MMA issuer (one lane): S_j = Q K_j^T into one of two TMEM
-//               buffers (M=128, N=128, K=128 as 8 x K16 steps, both operands
-//               K-major SW128 in shared memory), then O += P_{j-1} V_{j-1} with
-//               P read from TMEM and V as an MN-major SW128 operand.
-//               tcgen05.commit signals S ready, the K/V stage free, and O done.
-//   warps 0..3  softmax: thread t owns query row t = TMEM lane t.  It reads its
-//               row of S, masks (bottom-right causal, sequence end), keeps the
-//               running max in base 2, writes P (fp16/bf16) over the S buffer,
-//               and rescales its O row in TMEM only when the max grows by more
-//               than 2^8 (the max is a stabiliser; a stale one leaves the
-//               result exact).  The epilogue normalises O and writes O and LSE.
+//   producer    TMA: the Q tile once, then K and V tiles of 128 keys gathered
+//               through the block table (one 4-D TMA box per block and per 64
+//               columns of head_dim) into separate K and V rings; the block ids
+//               of a tile are fetched by 8-16 lanes at once, one tile ahead.
+//               Boxes past the sequence or of an out-of-pool block id are
+//               fetched at an out-of-range block coordinate (zero fill).
+//   MMA issuer  one lane: S = Q K^T (M=128, N=128, K=128 as 8 x K16 steps, both
+//               operands K-major SW128 in shared memory) and O += P V with P read
+//               from TMEM and V an MN-major SW128 operand; each 8-step product
+//               is one asm sequence.  tcgen05.commit signals S ready, ring
+//               stages free and O done.
+//   softmax     thread t owns query row t = TMEM lane t: masks (bottom-right
+//               causal, sequence end), keeps the running max in base 2, writes P
+//               (fp16/bf16) over S in TMEM, and rescales its O row only when the
+//               max grows by more than 2^8 (a stale max leaves the result
+//               exact).  A quarter of the exponentials run on the FMA pipe.  The
+//               epilogue normalises O and writes O and LSE.
 //
-// TMEM: S0 columns [0,128), S1 [128,256), O [256,384) of a 512-column
-// allocation; one CTA per SM (160 KB of shared memory).
+// pa_prefill_tc2_kernel (GQA groups of even size, the default): two query
+// heads of one KV head share every K/V tile; TMEM holds S_a, S_b, O_a, O_b.
+// pa_prefill_tc_kernel (one head): TMEM holds S0, S1 (double-buffered) and O;
+// each row's 128 columns are split between two softmax warpgroups.
 #include <atomic>
 #include <cstdlib>
 
@@ -35,14 +38,9 @@ namespace {
 constexpr int TC_BM = 128;        // query rows per CTA
 constexpr int TC_BN = 128;        // keys per tile
 constexpr int TC_D = 128;         // head_dim
-constexpr int TC_THREADS = 192;   // 4 softmax warps + producer + MMA
+constexpr int TC_THREADS = 320;   // 8 softmax warps (two per row) + producer + MMA
 constexpr int HALF_B = TC_BM * 128;               // one 64-column half of a 128-row tile: 16 KB
 constexpr int TILE_B = 2 * HALF_B;                // 32 KB
-constexpr int SQ_OFF = 0;
-constexpr int SK_OFF = TILE_B;                    // + stage * 2 * TILE_B
-constexpr int SV_OFF = 2 * TILE_B;
-constexpr int BAR_OFF = 5 * TILE_B;               // after Q + 2 stages of K and V
-constexpr int TC_SMEM = BAR_OFF + 256 + 1024;     // barriers + TMEM slot + alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 __device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
 constexpr uint32_t O_COL = 256;
@@ -54,10 +52,6 @@ constexpr float RESCALE_THRESHOLD = 8.0f;         // log2 units
 #define PA_EMU_EVERY_MASK 3
 #endif
 constexpr int EMU_EVERY_MASK = PA_EMU_EVERY_MASK;
-
-// barrier slots (8 bytes each) after BAR_OFF
-enum : int { B_QFULL = 0, B_QREADY = 1, B_KVFULL = 2, B_KVEMPTY = 4, B_SFULL = 6, B_PFULL = 8, B_ODONE = 10,
-             B_TMEMSLOT = 12 };
 
 struct alignas(64) TcMaps {
   CUtensorMap k;
@@ -80,6 +74,11 @@ __device__ __forceinline__ int tc_seq_keys(const AttnParams& p, int b, int q) {
   return static_cast<int>(nk);
 }
 
+// Named barrier `id` over `n` threads (the softmax warpgroups of a CTA).
+__device__ __forceinline__ void named_barrier_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory");
+}
+
 // Launch generation of the last launch in which a wait gave up: once one CTA
 // times out, every other wait of that launch stops within ~1k polls instead of
 // running into its own limit.
@@ -97,6 +96,17 @@ __device__ __noinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uin
   return false;
 }
 
+// Single-head kernel: K and V in separate 3-stage rings of 128-key tiles.
+constexpr int T1_KS = 3;
+constexpr int T1_VS = 3;
+constexpr int T1_K = TILE_B;                          // after Q
+constexpr int T1_V = T1_K + T1_KS * TILE_B;
+constexpr int T1_BAR = T1_V + T1_VS * TILE_B;         // 224 KB
+constexpr int T1_SMEM = T1_BAR + 256 + 1024 + 1024;  // barriers, row-max / row-sum exchange, alignment
+static_assert(T1_SMEM <= 227 * 1024, "shared memory per CTA");
+enum : int { E_QFULL = 0, E_QREADY = 1, E_KFULL = 2, E_KEMPTY = 5, E_VFULL = 8, E_VEMPTY = 11, E_SFULL = 14,
+             E_PFULL = 16, E_ODONE = 18, E_TMEMSLOT = 19 };
+
 template <bool MMA_BF16, bool Q_CONVERT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     pa_prefill_tc_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
@@ -112,7 +122,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sm = smem_raw + (base - raw);
-  const uint32_t bars = base + BAR_OFF;
+  const uint32_t bars = base + T1_BAR;
   auto bar = [&](int i) { return bars + 8u * i; };
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -125,112 +135,133 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
 
   if (tid == 0) {
-    mbar_init(bar(B_QFULL), 1);
-    mbar_init(bar(B_QREADY), 128);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(B_KVFULL + s), 1);
-      mbar_init(bar(B_KVEMPTY + s), 1);
-      mbar_init(bar(B_SFULL + s), 1);
-      mbar_init(bar(B_PFULL + s), 128);
+    mbar_init(bar(E_QFULL), 1);
+    mbar_init(bar(E_QREADY), 256);
+    for (int s = 0; s < T1_KS; ++s) {
+      mbar_init(bar(E_KFULL + s), 1);
+      mbar_init(bar(E_KEMPTY + s), 1);
     }
-    mbar_init(bar(B_ODONE), 1);
+    for (int s = 0; s < T1_VS; ++s) {
+      mbar_init(bar(E_VFULL + s), 1);
+      mbar_init(bar(E_VEMPTY + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(E_SFULL + s), 1);
+      mbar_init(bar(E_PFULL + s), 256);
+    }
+    mbar_init(bar(E_ODONE), 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
-    tmem_alloc(bar(B_TMEMSLOT), TMEM_COLS);
+  if (warp == 9) {
+    tmem_alloc(bar(E_TMEMSLOT), TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + BAR_OFF + 8 * B_TMEMSLOT);
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + T1_BAR + 8 * E_TMEMSLOT);
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && nt > 0) {
-      mbar_arrive_expect_tx(bar(B_QFULL), TILE_B);
-      tma_load_4d(base + SQ_OFF, &maps.q, bar(B_QFULL), 0, m0, hq, b);
-      tma_load_4d(base + SQ_OFF + HALF_B, &maps.q, bar(B_QFULL), 64, m0, hq, b);
+      mbar_arrive_expect_tx(bar(E_QFULL), TILE_B);
+      tma_load_4d(base, &maps.q, bar(E_QFULL), 0, m0, hq, b);
+      tma_load_4d(base + HALF_B, &maps.q, bar(E_QFULL), 64, m0, hq, b);
+    }
+    if (nt > 0) {
+      // Lane i owns box i of every tile: the block ids of a tile are fetched in
+      // one round trip (and one tile ahead), and each lane issues its own boxes.
       const int boxs = p.BS < 16 ? p.BS : 16;
-      const int nbox = TC_BN / boxs;
+      const int nbox = TC_BN / boxs;  // <= 16 (block_size >= 8)
       const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
-      for (int j = 0; j < nt; ++j) {
-        const int s = j & 1;
-        if (j >= 2) wait_or_flag(p, bar(B_KVEMPTY + s), ((j >> 1) - 1) & 1);
-        mbar_arrive_expect_tx(bar(B_KVFULL + s), 2 * TILE_B);
-        const uint32_t kdst = base + SK_OFF + s * 2 * TILE_B;
-        const uint32_t vdst = base + SV_OFF + s * 2 * TILE_B;
-        for (int i = 0; i < nbox; ++i) {
-          const int key = j * TC_BN + i * boxs;
-          int blk = p.NB;  // out of range: TMA fills the box with zeros
-          int slot = 0;
-          if (key < nkeys) {
-            const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
-            if (x >= 0 && x < p.NB) {
-              blk = x;
-              slot = key & (p.BS - 1);
-            } else {
-              set_status(p.status, ST_BAD_BLOCK_ID);
-            }
-          }
-          const uint32_t roff = static_cast<uint32_t>(i * boxs * 128);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tma_load_4d(kdst + h * HALF_B + roff, &maps.k, bar(B_KVFULL + s), 64 * h, kvh, slot, blk);
-            tma_load_4d(vdst + h * HALF_B + roff, &maps.v, bar(B_KVFULL + s), 64 * h, kvh, slot, blk);
-          }
+      auto fetch = [&](int j) {
+        const int key = j * TC_BN + lane * boxs;
+        int blk = p.NB;  // out of range: TMA fills the box with zeros
+        if (lane < nbox && key < nkeys) {
+          const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+          if (x >= 0 && x < p.NB) blk = x;
+          else set_status(p.status, ST_BAD_BLOCK_ID);
         }
+        return blk;
+      };
+      int blk = fetch(0);
+      for (int j = 0; j < nt; ++j) {
+        const int blk_next = (j + 1 < nt) ? fetch(j + 1) : p.NB;
+        const int slot = (j * TC_BN + lane * boxs) & (p.BS - 1);
+        const uint32_t roff = static_cast<uint32_t>(lane * boxs * 128);
+        const int ks = j % T1_KS;
+        const int vs = j % T1_VS;
+        if (lane == 0) {
+          if (j >= T1_KS) wait_or_flag(p, bar(E_KEMPTY + ks), ((j / T1_KS) - 1) & 1);
+          mbar_arrive_expect_tx(bar(E_KFULL + ks), TILE_B);
+        }
+        __syncwarp();
+        if (lane < nbox) {
+          const uint32_t dst = base + T1_K + ks * TILE_B + roff;
+          tma_load_4d(dst, &maps.k, bar(E_KFULL + ks), 0, kvh, blk < p.NB ? slot : 0, blk);
+          tma_load_4d(dst + HALF_B, &maps.k, bar(E_KFULL + ks), 64, kvh, blk < p.NB ? slot : 0, blk);
+        }
+        if (lane == 0) {
+          if (j >= T1_VS) wait_or_flag(p, bar(E_VEMPTY + vs), ((j / T1_VS) - 1) & 1);
+          mbar_arrive_expect_tx(bar(E_VFULL + vs), TILE_B);
+        }
+        __syncwarp();
+        if (lane < nbox) {
+          const uint32_t dst = base + T1_V + vs * TILE_B + roff;
+          tma_load_4d(dst, &maps.v, bar(E_VFULL + vs), 0, kvh, blk < p.NB ? slot : 0, blk);
+          tma_load_4d(dst + HALF_B, &maps.v, bar(E_VFULL + vs), 64, kvh, blk < p.NB ? slot : 0, blk);
+        }
+        blk = blk_next;
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nt > 0) {
       constexpr uint32_t IDESC_QK = instr_desc_f16(MMA_BF16, false, false, TC_BM, TC_BN);
       constexpr uint32_t IDESC_PV = instr_desc_f16(MMA_BF16, false, true, TC_BM, TC_D);
-      auto issue_pv = [&](int jj) {
-        const int s = jj & 1;
-        wait_or_flag(p, bar(B_PFULL + s), (jj >> 1) & 1);
+      auto pv = [&](int jj) {
+        wait_or_flag(p, bar(E_PFULL + (jj & 1)), (jj >> 1) & 1);
+        wait_or_flag(p, bar(E_VFULL + jj % T1_VS), (jj / T1_VS) & 1);
         tc_fence_after();
-        const uint32_t vbase = base + SV_OFF + s * 2 * TILE_B;
-#pragma unroll
-        for (int k = 0; k < TC_BN / 16; ++k) {
-          // V: MN-major SW128; LBO = distance between the two 64-column halves, SBO = 8 rows
-          const uint64_t bdesc = smem_desc(vbase + k * 16 * 128, HALF_B, 1024);
-          tc_mma_ts(tmem + O_COL, tmem + s_col(s) + 8 * k, bdesc, IDESC_PV, (jj > 0 || k > 0) ? 1u : 0u);
-        }
-        tc_commit(bar(B_KVEMPTY + s));
-        tc_commit(bar(B_ODONE));
+        tc_mma_ts_seq<TC_BN / 16>(tmem + O_COL, tmem + s_col(jj & 1),
+                                  smem_desc(base + T1_V + (jj % T1_VS) * TILE_B, HALF_B, 1024), IDESC_PV,
+                                  jj > 0 ? 1u : 0u);
+        tc_commit(bar(E_VEMPTY + jj % T1_VS));
+        tc_commit(bar(E_ODONE));
       };
-      wait_or_flag(p, bar(B_QREADY), 0);
-      tc_fence_after();
+      wait_or_flag(p, bar(E_QREADY), 0);
       for (int j = 0; j < nt; ++j) {
-        const int s = j & 1;
-        wait_or_flag(p, bar(B_KVFULL + s), (j >> 1) & 1);
+        // S_j into buffer j % 2 (its previous P was consumed by a P*V issued earlier)
+        wait_or_flag(p, bar(E_KFULL + j % T1_KS), (j / T1_KS) & 1);
         tc_fence_after();
-        const uint32_t kbase = base + SK_OFF + s * 2 * TILE_B;
-#pragma unroll
-        for (int k = 0; k < TC_D / 16; ++k) {
-          // K-major SW128: a K16 step advances 32 bytes inside the 128-byte row
-          const uint32_t koff = (k >> 2) * HALF_B + (k & 3) * 32;
-          tc_mma_ss(tmem + s_col(s), smem_desc(base + SQ_OFF + koff, 16, 1024), smem_desc(kbase + koff, 16, 1024),
-                    IDESC_QK, k > 0 ? 1u : 0u);
-        }
-        tc_commit(bar(B_SFULL + s));
-        if (j > 0) issue_pv(j - 1);
+        tc_mma_ss_k128<HALF_B / 16, HALF_B / 16>(tmem + s_col(j & 1), smem_desc(base, 16, 1024),
+                                                 smem_desc(base + T1_K + (j % T1_KS) * TILE_B, 16, 1024), IDESC_QK);
+        tc_commit(bar(E_SFULL + (j & 1)));
+        tc_commit(bar(E_KEMPTY + j % T1_KS));
+        if (j > 0) pv(j - 1);
       }
-      issue_pv(nt - 1);
+      pv(nt - 1);
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0..3)
-    const int row = m0 + tid;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // ------------------------------------------------------------ softmax (warps 0..7)
+    // Two warpgroups share every row: warp w serves TMEM lanes 32 (w % 4) ..,
+    // warpgroup 0 the keys [0, 64) of each tile, warpgroup 1 the keys [64, 128).
+    // Row maxima are combined through shared memory at a named barrier of the
+    // 256 softmax threads, which also orders both halves' S loads before either
+    // overwrites S with P.  Each half keeps its own row sum and rescales and
+    // stores its own 64 columns of O.
+    const int hf = warp >> 2;           // column half
+    const int r = tid & 127;            // query row within the tile = TMEM lane
+    const int row = m0 + r;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    float* mxs = reinterpret_cast<float*>(sm + T1_BAR + 256);  // [2 halves][128 rows]
     if (nt > 0) {
-      wait_or_flag(p, bar(B_QFULL), 0);
+      wait_or_flag(p, bar(E_QFULL), 0);
       if constexpr (Q_CONVERT) {
         // Q arrives in its own 16-bit type; convert in place to the pool's type
-        uint4* q4 = reinterpret_cast<uint4*>(sm + SQ_OFF);
+        uint4* q4 = reinterpret_cast<uint4*>(sm);
 #pragma unroll 4
-        for (int i = tid; i < TILE_B / 16; i += 128) {
+        for (int i = tid; i < TILE_B / 16; i += 256) {
           uint4 v = q4[i];
           v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
           v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
@@ -240,7 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         fence_proxy_async_smem();
       }
-      mbar_arrive(bar(B_QREADY));
+      mbar_arrive(bar(E_QREADY));
     }
     const int lim = min(nkeys, off + row + 1);
     float m_ref = -INFINITY;
@@ -250,122 +281,159 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // once, one on a phase two behind never does.
     int od = 0;
     auto wait_o_done = [&](int k) {
-      for (; od <= k; ++od) wait_or_flag(p, bar(B_ODONE), od & 1);
+      for (; od <= k; ++od) wait_or_flag(p, bar(E_ODONE), od & 1);
     };
     for (int j = 0; j < nt; ++j) {
       const int s = j & 1;
-      wait_or_flag(p, bar(B_SFULL + s), (j >> 1) & 1);
+      wait_or_flag(p, bar(E_SFULL + s), (j >> 1) & 1);
       tc_fence_after();
-      float x[TC_BN];
+      const uint32_t scol = s_col(s);
+      const int k0 = j * TC_BN + 64 * hf;  // first key of this half
+      const bool need_mask = (k0 + 64 > off + m0 + 1) || (k0 + 64 > nkeys);
+      // this half's 64 logits of the row (masked entries -inf) and their max
+      uint32_t r0[32], r1[32];
+      tmem_ld32(trow + scol + 64 * hf, r0);
+      tmem_ld32(trow + scol + 64 * hf + 32, r1);
+      tmem_wait_ld();
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < TC_BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + s_col(s) + 32 * c, r);
-        tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) {
+          const float v0 = (k0 + i < lim) ? __uint_as_float(r0[i]) : -INFINITY;
+          const float v1 = (k0 + 32 + i < lim) ? __uint_as_float(r1[i]) : -INFINITY;
+          r0[i] = __float_as_uint(v0);
+          r1[i] = __float_as_uint(v1);
+          mx4[i & 3] = fmax3f(mx4[i & 3], v0, v1);
+        }
+      } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[32 * c + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(r0[i]), __uint_as_float(r1[i]));
       }
-      const int k0 = j * TC_BN;
-      const bool need_mask = (k0 + TC_BN > off + m0 + 1) || (k0 + TC_BN > nkeys);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < TC_BN; ++i) {
-        float v = x[i] * p.scale_log2;
-        if (need_mask && k0 + i >= lim) v = -INFINITY;
-        x[i] = v;
-        mx = fmaxf(mx, v);
-      }
+      const float mhalf = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      mxs[hf * 128 + r] = mhalf;
+      named_barrier_sync(2, 256);
+      const float mx = fmaxf(mhalf, mxs[(hf ^ 1) * 128 + r]) * p.scale_log2;
+      named_barrier_sync(2, 256);  // both halves have read before the next write
       float alpha = 1.f;
       bool resc = false;
       if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
         alpha = ex2(m_ref - mx);
-        resc = l > 0.f;
+        resc = l > 0.f;  // the same decision in both halves (same max, same history)
         m_ref = mx;
       }
       if (__any_sync(0xffffffffu, resc)) {
-        // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this row
+        // O holds P_0..P_{j-1} V: wait for the last of them, then rescale this half of the row
         wait_o_done(j - 1);
         tc_fence_after();
         const float a = resc ? alpha : 1.f;
 #pragma unroll
-        for (int c = 0; c < TC_D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(trow + O_COL + 32 * c, r);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(trow + O_COL + 64 * hf + 32 * c, rr);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * a);
-          tmem_st32(trow + O_COL + 32 * c, r);
+          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
+          tmem_st32(trow + O_COL + 64 * hf + 32 * c, rr);
         }
         tmem_wait_st();
       }
       l *= alpha;
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      const float c2 = p.scale_log2;
+      // P = 2^(s*c - m) packed in pairs from the registers; P of keys
+      // [64 hf, 64 hf + 64) goes to TMEM columns [32 hf, 32 hf + 32) of the S buffer
+      uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+      uint32_t pk[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[32];
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t* rr = h ? r1 : r0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2(x[64 * c + 2 * i] - m_use);
-          const float p1 = ex2(x[64 * c + 2 * i + 1] - m_use);
-          l += p0 + p1;
-          pk[i] = pack2<MMA_BF16>(p0, p1);
+        for (int i = 0; i < 16; ++i) {
+          float p0, p1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                           f2_pack(neg_m, neg_m)),
+                    p0, p1);
+          if ((i & EMU_EVERY_MASK) == EMU_EVERY_MASK) {
+            exp2_fma_x2(p0, p1);  // this share of the exponentials runs on the FMA pipe
+          } else {
+            p0 = ex2(p0);
+            p1 = ex2(p1);
+          }
+          if (need_mask) {
+            const int kk = k0 + 32 * h + 2 * i;
+            if (kk >= lim) p0 = 0.f;
+            if (kk + 1 >= lim) p1 = 0.f;
+          }
+          lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
+          pk[16 * h + i] = pack2<MMA_BF16>(p0, p1);
         }
-        tmem_st32(trow + s_col(s) + 32 * c, pk);
+      }
+      tmem_st32(trow + scol + 32 * hf, pk);
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(lsum2[0], a0, a1);
+        f2_unpack(lsum2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
       }
       tmem_wait_st();
-      if (nkeys - k0 < TC_BN) {
-        // keys past the sequence: zero their V rows so that P = 0 contributes
-        // exactly nothing even if the pool slots hold non-finite bytes
-        if (k0 + tid >= nkeys) {
-          unsigned char* vrow = sm + SV_OFF + s * 2 * TILE_B + tid * 128;
+      const int kt = j * TC_BN;
+      if (nkeys - kt < TC_BN) {
+        // keys past the sequence: zero their V rows (each half zeroes its
+        // 64-column half of the row) so that P = 0 contributes exactly nothing
+        wait_or_flag(p, bar(E_VFULL + j % T1_VS), (j / T1_VS) & 1);
+        if (kt + r >= nkeys) {
+          unsigned char* vrow = sm + T1_V + (j % T1_VS) * TILE_B + hf * HALF_B + r * 128;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + h * HALF_B + 16 * c) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async_smem();
       }
       // stay within one phase of the O-done barrier (P*V(j-1) finished long ago)
       if (j >= 1) wait_o_done(j - 1);
       tc_fence_before();
-      mbar_arrive(bar(B_PFULL + s));
+      mbar_arrive(bar(E_PFULL + s));
     }
     // ---- epilogue: O / l, LSE ---------------------------------------------
+    // the row sum is the sum of the two halves' sums
+    mxs[hf * 128 + r] = l;
+    named_barrier_sync(2, 256);
+    const float lt = l + mxs[(hf ^ 1) * 128 + r];
     const bool valid = row < qlen;
-    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
+    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
+                   64 * hf;
     if (nt > 0) {
       wait_o_done(nt - 1);
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
-      for (int c = 0; c < TC_D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + O_COL + 32 * c, r);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t rr[32];
+        tmem_ld32(trow + O_COL + 64 * hf + 32 * c, rr);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             uint4 w;
-            w.x = pack_f16(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
-            w.y = pack_f16(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
-            w.z = pack_f16(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
-            w.w = pack_f16(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+            w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+            w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+            w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+            w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
             *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
           }
         }
       }
     } else if (valid) {
-      for (int d = 0; d < TC_D; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+      for (int d = 0; d < 64; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
     }
-    if (valid && p.lse) {
-      const float L = l > 0.f ? (m_ref + lg2(l)) * 0.6931471805599453f : -INFINITY;
+    if (valid && p.lse && hf == 0) {
+      const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
       static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
           __float2half_rn(L);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -513,22 +581,16 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       auto qk = [&](int x, int j) {
         const uint32_t kb = base + P2_K + (j % P2_KS) * TILE_B;
         const uint32_t qb = base + (x ? P2_QB : P2_QA);
-#pragma unroll
-        for (int k = 0; k < TC_D / 16; ++k) {
-          const uint32_t koff = (k >> 2) * HALF_B + (k & 3) * 32;
-          tc_mma_ss(tmem + s_col(x), smem_desc(qb + koff, 16, 1024), smem_desc(kb + koff, 16, 1024), IDESC_QK,
-                    k > 0 ? 1u : 0u);
-        }
+        tc_mma_ss_k128<HALF_B / 16, HALF_B / 16>(tmem + s_col(x), smem_desc(qb, 16, 1024), smem_desc(kb, 16, 1024),
+                                                 IDESC_QK);
         tc_commit(bar(C_SFULL + x));
       };
       auto pv = [&](int x, int j) {
         wait_or_flag(p, bar(C_PFULL + x), j & 1);
         tc_fence_after();
         const uint32_t vb = base + P2_V + (j % P2_VS) * TILE_B;
-#pragma unroll
-        for (int k = 0; k < TC_BN / 16; ++k)
-          tc_mma_ts(tmem + O_COL + 128 * x, tmem + s_col(x) + 8 * k, smem_desc(vb + k * 16 * 128, HALF_B, 1024),
-                    IDESC_PV, (j > 0 || k > 0) ? 1u : 0u);
+        tc_mma_ts_seq<TC_BN / 16>(tmem + O_COL + 128 * x, tmem + s_col(x), smem_desc(vb, HALF_B, 1024), IDESC_PV,
+                                  j > 0 ? 1u : 0u);
         tc_commit(bar(C_ODONE + x));
       };
       wait_or_flag(p, bar(C_QREADY), 0);
@@ -774,9 +836,9 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
   }
   const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);
   auto launch = [&](auto kern) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T1_SMEM);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(kern, grid, dim3(TC_THREADS), TC_SMEM, stream, p, maps);
+    e = launch_pdl(kern, grid, dim3(TC_THREADS), T1_SMEM, stream, p, maps);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };
