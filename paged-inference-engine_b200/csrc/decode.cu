@@ -48,7 +48,7 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr int META_B = 16;      // per stage: [0] fp16 half-select mask of the scale words, [1] missing rows
 // Shared-memory bytes of tile ring per warp (16-bit pools / int8 pools).
 #ifndef PA_DEC_STAGE_BUDGET
-#define PA_DEC_STAGE_BUDGET (26 * 1024)
+#define PA_DEC_STAGE_BUDGET (22 * 1024)
 #endif
 #ifndef PA_DEC_STAGE_BUDGET_I8
 #define PA_DEC_STAGE_BUDGET_I8 (17 * 1024)
