@@ -16,15 +16,15 @@
 //               from TMEM and V an MN-major SW128 operand; each 8-step product
 //               is one asm sequence.  tcgen05.commit signals S ready, ring
 //               stages free and O done.
-//   softmax     thread t owns query row t = TMEM lane t: masks (bottom-right
-//               causal, sequence end), keeps the running max in base 2, writes P
-//               (fp16/bf16) over S in TMEM, and rescales its O row only when the
+//   softmax     the threads of query row t (TMEM lane t) mask it (bottom-right
+//               causal, sequence end), keep its running max in base 2, write P
+//               (fp16/bf16) over S in TMEM, and rescale its O row only when the
 //               max grows by more than 2^8 (a stale max leaves the result
-//               exact).  A quarter of the exponentials run on the FMA pipe.  The
-//               epilogue normalises O and writes O and LSE.
+//               exact).  The epilogue normalises O and writes O and LSE.
 //
 // pa_prefill_tc2_kernel (GQA groups of even size, the default): two query
-// heads of one KV head share every K/V tile; TMEM holds S_a, S_b, O_a, O_b.
+// heads of one KV head share every K/V tile; TMEM holds S_a, S_b, O_a, O_b;
+// each row of each head is split between two softmax warps (64 keys each).
 // pa_prefill_tc_kernel (one head): TMEM holds S0, S1 (double-buffered) and O;
 // each row's 128 columns are split between two softmax warpgroups.
 #include <atomic>
@@ -45,13 +45,20 @@ constexpr uint32_t TMEM_COLS = 512;
 __device__ __forceinline__ constexpr uint32_t s_col(int s) { return s ? 128u : 0u; }
 constexpr uint32_t O_COL = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;         // log2 units
-// Pairs of probabilities whose index i satisfies (i & MASK) == MASK compute
-// 2^x with the FMA-pipe polynomial instead of MUFU.EX2 (MUFU throughput per SM
-// matches the tensor core's rate per score element for head_dim 128).
+// With PA_EMU_EVERY_MASK = M >= 0, pairs of probabilities whose index i
+// satisfies (i & M) == M compute 2^x with the FMA-pipe polynomial instead of
+// MUFU.EX2 (MUFU throughput per SM matches the tensor core's rate per score
+// element for head_dim 128).  Off by default: measured on B200, every kernel
+// here is faster with all exponentials on MUFU (paired heads 674 against 642
+// TFLOP/s with a quarter on the FMA pipe); the polynomial's instructions cost
+// more issue slots than the MUFU queue wait they save.
 #ifndef PA_EMU_EVERY_MASK
-#define PA_EMU_EVERY_MASK 3
+#define PA_EMU_EVERY_MASK -1
 #endif
 constexpr int EMU_EVERY_MASK = PA_EMU_EVERY_MASK;
+__device__ __forceinline__ constexpr bool emu_pair(int i) {
+  return EMU_EVERY_MASK >= 0 && (i & EMU_EVERY_MASK) == EMU_EVERY_MASK;
+}
 
 struct alignas(64) TcMaps {
   CUtensorMap k;
@@ -84,8 +91,10 @@ __device__ __forceinline__ void named_barrier_sync(int id, int n) {
 // running into its own limit.
 __device__ unsigned int g_tc_abort_gen = 0;
 
-// Bounded mbarrier wait; false (and a status bit) on time-out or abort.
-__device__ __noinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uint32_t parity) {
+// Bounded mbarrier wait; false (and a status bit) on time-out or abort.  The
+// first poll is inlined: a wait on a phase that has already completed costs
+// ~55 cycles this way against ~240 through the out-of-line loop.
+__device__ __noinline__ bool wait_or_flag_slow(const AttnParams& p, uint32_t bar, uint32_t parity) {
   constexpr int kLimit = 1 << 20;
   for (int i = 0; i < kLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -94,6 +103,10 @@ __device__ __noinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uin
   atomicExch(&g_tc_abort_gen, p.abort_gen);
   set_status(p.status, ST_WAIT_TIMEOUT);
   return false;
+}
+__device__ __forceinline__ bool wait_or_flag(const AttnParams& p, uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return wait_or_flag_slow(p, bar, parity);
 }
 
 // Single-head kernel: K and V in separate 3-stage rings of 128-key tiles.
@@ -318,7 +331,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       bool resc = false;
       if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
         alpha = ex2(m_ref - mx);
-        resc = l > 0.f;  // the same decision in both halves (same max, same history)
+        // O holds P*V of earlier tiles once j > 0, whatever this half's own sum
+        // is (every probability of a half can underflow): both halves decide
+        // alike from the shared maximum.
+        resc = j > 0;
         m_ref = mx;
       }
       if (__any_sync(0xffffffffu, resc)) {
@@ -353,8 +369,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
                            f2_pack(neg_m, neg_m)),
                     p0, p1);
-          if ((i & EMU_EVERY_MASK) == EMU_EVERY_MASK) {
-            exp2_fma_x2(p0, p1);  // this share of the exponentials runs on the FMA pipe
+          if (emu_pair(i)) {
+            exp2_fma_x2(p0, p1);  // optionally a share of the exponentials on the FMA pipe
           } else {
             p0 = ex2(p0);
             p1 = ex2(p1);
@@ -441,16 +457,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Paired-head variant (grouped-query attention with an even group): one CTA
+// Paired-head kernel (grouped-query attention with an even group): one CTA
 // computes the same 128 query rows for two query heads of one KV group, so each
-// K/V tile is fetched once for both.  Two softmax warpgroups (warps 0-3: head a,
-// 4-7: head b) alternate with the tensor core: while one warpgroup turns S into
-// P, the MMA warp runs the other head's P*V and next Q*K^T ("ping-pong").
-// K and V have separate rings (3 and 2 stages) so a K stage is recycled as soon
-// as both Q*K^T products have consumed it.  TMEM: S_a [0,128), S_b [128,256),
+// K/V tile is fetched once for both.  The softmax warps of the two heads
+// alternate with the tensor core: while one head turns S into P, the MMA warp
+// runs the other head's P*V and next Q*K^T ("ping-pong").  K and V have
+// separate rings (3 and 2 stages) so a K stage is recycled as soon as both
+// Q*K^T products have consumed it.  TMEM: S_a [0,128), S_b [128,256),
 // O_a [256,384), O_b [384,512).
+//
+// Warp w < 16 serves TMEM lanes 32 (w % 4) .. of head (w >> 2) & 1 and the
+// keys [64 h, 64 h + 64) of every tile, h = w >> 3: each sub-partition runs
+// two warps per head, so one warp's independent work issues while the other
+// waits on MUFU, and each warp reads its 64 logits from TMEM once.  Row maxima
+// are combined through shared memory at a named barrier of the head's 256
+// threads (half 1 posts its maximum, half 0 posts the row's), which also
+// orders both halves' S loads before either overwrites S with P.
 // ---------------------------------------------------------------------------
-constexpr int P2_THREADS = 320;   // 2 softmax warpgroups + producer + MMA
 constexpr int P2_KS = 3;          // K stages
 constexpr int P2_VS = 2;          // V stages
 constexpr int P2_QA = 0;
@@ -458,9 +481,15 @@ constexpr int P2_QB = TILE_B;
 constexpr int P2_K = 2 * TILE_B;
 constexpr int P2_V = P2_K + P2_KS * TILE_B;
 constexpr int P2_BAR = P2_V + P2_VS * TILE_B;     // 224 KB
-constexpr int P2_SMEM = P2_BAR + 256 + 1024;
 enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, C_VEMPTY = 10, C_SFULL = 12,
              C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18 };
+
+constexpr int P2_THREADS = 576;   // 16 softmax warps + producer + MMA
+constexpr int P2_PRODUCER = 16;
+constexpr int P2_MMA = 17;
+constexpr int P2_XCH = P2_BAR + 256;              // float [2 heads][128 rows]
+constexpr int P2_SMEM = P2_XCH + 1024 + 1024;      // + alignment slack
+static_assert(P2_SMEM <= 227 * 1024, "shared memory per CTA");
 
 template <bool MMA_BF16, bool Q_CONVERT>
 __global__ void __launch_bounds__(P2_THREADS, 1)
@@ -492,7 +521,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
 
   if (tid == 0) {
     mbar_init(bar(C_QFULL), 1);
-    mbar_init(bar(C_QREADY), 256);
+    mbar_init(bar(C_QREADY), 512);
     for (int s = 0; s < P2_KS; ++s) {
       mbar_init(bar(C_KFULL + s), 1);
       mbar_init(bar(C_KEMPTY + s), 1);
@@ -503,12 +532,12 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(C_SFULL + x), 1);
-      mbar_init(bar(C_PFULL + x), 128);
+      mbar_init(bar(C_PFULL + x), 256);
       mbar_init(bar(C_ODONE + x), 1);
     }
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == P2_MMA) {
     tmem_alloc(bar(C_TMEMSLOT), TMEM_COLS);
     tmem_relinquish();
   }
@@ -517,7 +546,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + P2_BAR + 8 * C_TMEMSLOT);
 
-  if (warp == 8) {
+  if (warp == P2_PRODUCER) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && nt > 0) {
       mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
@@ -528,8 +557,6 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       }
     }
     if (nt > 0) {
-      // Lane i owns box i of every tile: the block ids of a tile are fetched in
-      // one round trip (and one tile ahead), and each lane issues its own boxes.
       const int boxs = p.BS < 16 ? p.BS : 16;
       const int nbox = TC_BN / boxs;  // <= 16 (block_size >= 8)
       const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
@@ -573,7 +600,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         blk = blk_next;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == P2_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nt > 0) {
       constexpr uint32_t IDESC_QK = instr_desc_f16(MMA_BF16, false, false, TC_BM, TC_BN);
@@ -617,19 +644,22 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0-7)
-    const int x = warp >> 2;     // 0: head a, 1: head b
-    const int r = tid & 127;     // query row within the tile = TMEM lane
+    // ------------------------------------------------------------ softmax (warps 0-15)
+    const int x = (warp >> 2) & 1;  // 0: head a, 1: head b
+    const int hf = warp >> 3;       // key half of every tile
+    const int r = tid & 127;        // query row within the tile = TMEM lane
     const int row = m0 + r;
+    const int bar_id = 1 + x;       // named barrier of this head's 256 threads
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t scol = s_col(x);
-    const uint32_t ocol = O_COL + 128 * x;
+    const uint32_t ocol = O_COL + 128 * x + 64 * hf;
+    float* xch = reinterpret_cast<float*>(sm + P2_XCH) + x * 128 + r;
     if (nt > 0) {
       wait_or_flag(p, bar(C_QFULL), 0);
       if constexpr (Q_CONVERT) {
         uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
 #pragma unroll 4
-        for (int i = r; i < TILE_B / 16; i += 128) {
+        for (int i = hf * 128 + r; i < TILE_B / 16; i += 256) {
           uint4 v = q4[i];
           v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
           v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
@@ -641,55 +671,105 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       }
       mbar_arrive(bar(C_QREADY));
     }
+    // Half 1 posts a value, half 0 combines it with its own and posts the
+    // result, half 1 reads it back: two barriers, one float per row and head.
+    auto combine = [&](float v, bool is_max) {
+      if (hf) {
+        *xch = v;
+        named_barrier_sync(bar_id, 256);
+        named_barrier_sync(bar_id, 256);
+        return *xch;
+      }
+      named_barrier_sync(bar_id, 256);
+      const float o = *xch;
+      const float t = is_max ? fmaxf(v, o) : v + o;
+      *xch = t;
+      named_barrier_sync(bar_id, 256);
+      return t;
+    };
     const int lim = min(nkeys, off + row + 1);
     float m_ref = -INFINITY;
     float l = 0.f;
-    // O-done phases are consumed one by one and never more than one phase
-    // away from the barrier: a parity wait on a phase two ahead succeeds at
-    // once, one on a phase two behind never does.
-    int od = 0;
-    auto wait_o_done = [&](int k) {
-      for (; od <= k; ++od) wait_or_flag(p, bar(C_ODONE + x), od & 1);
-    };
+    // The MMA warp issues Q*K^T(x, j+1) after P*V(x, j), and a tcgen05.commit
+    // arrives only once every earlier tcgen05 operation of its thread has
+    // completed: S(x, j) ready implies P*V(x, j-1) done.  O-done is therefore
+    // waited on once, for the last P*V, in the epilogue.
     for (int j = 0; j < nt; ++j) {
       wait_or_flag(p, bar(C_SFULL + x), j & 1);
       tc_fence_after();
-      const int k0 = j * TC_BN;
-      const bool need_mask = (k0 + TC_BN > off + m0 + 1) || (k0 + TC_BN > nkeys);
-      // pass 1: row max of the raw logits (the scale is positive), masked on
-      // diagonal / sequence-end tiles; two TMEM loads in flight per wait
-      float mraw = -INFINITY;
+      const int k0 = j * TC_BN + 64 * hf;  // first key of this half
+      const bool need_mask = (k0 + 64 > off + m0 + 1) || (k0 + 64 > nkeys);
+      uint32_t r0[32], r1[32];
+      tmem_ld32(trow + scol + 64 * hf, r0);
+      tmem_ld32(trow + scol + 64 * hf + 32, r1);
+      tmem_wait_ld();
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < TC_BN / 64; ++c) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(trow + scol + 64 * c, r0);
-        tmem_ld32(trow + scol + 64 * c + 32, r1);
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (k0 + 64 * c + i < lim) mraw = fmaxf(mraw, __uint_as_float(r0[i]));
-            if (k0 + 64 * c + 32 + i < lim) mraw = fmaxf(mraw, __uint_as_float(r1[i]));
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mraw = fmax3f(mraw, __uint_as_float(r0[i]), __uint_as_float(r1[i]));
+        for (int i = 0; i < 32; ++i) {
+          const float v0 = (k0 + i < lim) ? __uint_as_float(r0[i]) : -INFINITY;
+          const float v1 = (k0 + 32 + i < lim) ? __uint_as_float(r1[i]) : -INFINITY;
+          r0[i] = __float_as_uint(v0);
+          r1[i] = __float_as_uint(v1);
+          mx4[i & 3] = fmax3f(mx4[i & 3], v0, v1);
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(r0[i]), __uint_as_float(r1[i]));
       }
-      const float mx = mraw * p.scale_log2;
+      const float mx = combine(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), true) * p.scale_log2;
       float alpha = 1.f;
       bool resc = false;
-      if (mx > m_ref + RESCALE_THRESHOLD) {
+      if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
         alpha = ex2(m_ref - mx);
-        resc = l > 0.f;
+        // O holds P*V of earlier tiles once j > 0, whatever this half's own sum
+        // is: both halves decide alike from the shared maximum.
+        resc = j > 0;
         m_ref = mx;
       }
-      if (__any_sync(0xffffffffu, resc)) {
-        wait_o_done(j - 1);
-        tc_fence_after();
+      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+      const float c2 = p.scale_log2;
+      // P of keys [64 hf + 16 q, +16) goes to TMEM columns [32 hf + 8 q, +8) of S
+      uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int h = q >> 1;
+        const uint32_t* rr = (h ? r1 : r0) + 16 * (q & 1);
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float p0, p1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                           f2_pack(neg_m, neg_m)),
+                    p0, p1);
+          if (emu_pair(i)) {
+            exp2_fma_x2(p0, p1);
+          } else {
+            p0 = ex2(p0);
+            p1 = ex2(p1);
+          }
+          if (need_mask) {
+            const int kk = k0 + 16 * q + 2 * i;
+            if (kk >= lim) p0 = 0.f;
+            if (kk + 1 >= lim) p1 = 0.f;
+          }
+          lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
+          pk[i] = pack2<MMA_BF16>(p0, p1);
+        }
+        tmem_st8(trow + scol + 32 * hf + 8 * q, pk);
+      }
+      {
+        float a0, a1, b0, b1;
+        f2_unpack(lsum2[0], a0, a1);
+        f2_unpack(lsum2[1], b0, b1);
+        l = l * alpha + ((a0 + a1) + (b0 + b1));
+      }
+      // Rescale this half's O columns after the logits are dead (fewer live
+      // registers); P*V(j) is issued only after PFULL, so O is still P*V(<j).
+      if (__any_sync(0xffffffffu, resc)) {  // O holds P*V(<j), complete (see above)
         const float a = resc ? alpha : 1.f;
 #pragma unroll
-        for (int c = 0; c < TC_D / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t rr[32];
           tmem_ld32(trow + ocol + 32 * c, rr);
           tmem_wait_ld();
@@ -697,79 +777,35 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
           for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
           tmem_st32(trow + ocol + 32 * c, rr);
         }
-        tmem_wait_st();
-      }
-      l *= alpha;
-      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
-      const float c2 = p.scale_log2;
-      // pass 2: P = 2^(s*c - m) packed in pairs over the S columns already read
-      uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};  // packed pairs, two chains
-#pragma unroll
-      for (int c = 0; c < TC_BN / 64; ++c) {
-        uint32_t r0[32], r1[32], pk[32];
-        tmem_ld32(trow + scol + 64 * c, r0);
-        tmem_ld32(trow + scol + 64 * c + 32, r1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t* rr = h ? r1 : r0;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float p0, p1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
-                             f2_pack(neg_m, neg_m)),
-                      p0, p1);
-            if ((i & EMU_EVERY_MASK) == EMU_EVERY_MASK) {
-              exp2_fma_x2(p0, p1);  // this share of the exponentials runs on the FMA pipe
-            } else {
-              p0 = ex2(p0);
-              p1 = ex2(p1);
-            }
-            if (need_mask) {
-              const int kk = k0 + 64 * c + 32 * h + 2 * i;
-              if (kk >= lim) p0 = 0.f;
-              if (kk + 1 >= lim) p1 = 0.f;
-            }
-            lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
-            pk[16 * h + i] = pack2<MMA_BF16>(p0, p1);
-          }
-        }
-        tmem_st32(trow + scol + 32 * c, pk);
-      }
-      {
-        float a0, a1, b0, b1;
-        f2_unpack(lsum2[0], a0, a1);
-        f2_unpack(lsum2[1], b0, b1);
-        l += (a0 + a1) + (b0 + b1);
       }
       tmem_wait_st();
-      if (x == 0 && nkeys - k0 < TC_BN) {
-        // keys past the sequence: zero their V rows (head a's P*V runs first)
+      const int kt = j * TC_BN;
+      if (x == 0 && nkeys - kt < TC_BN) {
+        // keys past the sequence: zero their V rows (head a's P*V runs first;
+        // each half zeroes its 64-column half of the row)
         wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
-        if (k0 + r >= nkeys) {
-          unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + r * 128;
+        if (kt + r >= nkeys) {
+          unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + hf * HALF_B + r * 128;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + h * HALF_B + 16 * c) = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async_smem();
       }
-      // stay within one phase of the O-done barrier (P*V(j-1) finished long ago)
-      if (j >= 1) wait_o_done(j - 1);
       tc_fence_before();
       mbar_arrive(bar(C_PFULL + x));
     }
-    // ---- epilogue ------------------------------------------------------------
+    // ---- epilogue: O / l, LSE ---------------------------------------------
+    const float lt = combine(l, false);
     const int hq = hq0 + x;
     const bool valid = row < qlen;
-    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
+    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
+                   64 * hf;
     if (nt > 0) {
-      wait_o_done(nt - 1);
+      wait_or_flag(p, bar(C_ODONE + x), (nt - 1) & 1);  // the last P*V (phase nt-1)
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
-      for (int c = 0; c < TC_D / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t rr[32];
         tmem_ld32(trow + ocol + 32 * c, rr);
         tmem_wait_ld();
@@ -786,17 +822,17 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         }
       }
     } else if (valid) {
-      for (int d = 0; d < TC_D; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+      for (int d = 0; d < 64; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
     }
-    if (valid && p.lse) {
-      const float L = l > 0.f ? (m_ref + lg2(l)) * 0.6931471805599453f : -INFINITY;
+    if (valid && p.lse && hf == 0) {
+      const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
       static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
           __float2half_rn(L);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == P2_MMA) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -831,7 +867,8 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
       if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
-    if (mma_bf16) return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
+    if (mma_bf16)
+      return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
     return convert ? launch2(pa_prefill_tc2_kernel<false, true>) : launch2(pa_prefill_tc2_kernel<false, false>);
   }
   const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);

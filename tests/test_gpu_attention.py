@@ -219,6 +219,50 @@ def test_rising_logits_vs_oracle(fa, kv, mode):
     _compare(O, L, O_or, L_or, q_len.numpy(), TOL_I8 if kv == "i8" else TOL_F16, f"rising {kv} {mode}")
 
 
+@pytest.mark.parametrize("kernel", ["paired", "single"])
+def test_extreme_logit_range_prefill(fa, kernel, monkeypatch):
+    """Causal prefill where the keys of the first 64 of every 128 are ~140
+    log2 units below the others (their probabilities underflow), and keys of
+    the second tile sit ~30 log2 units above the first tile's maximum (every
+    row's O is rescaled at tile 1).  Run on the paired-head tensor-core kernel
+    (even GQA group) and on the single-head one."""
+    if kernel == "single":
+        monkeypatch.setenv("PIE_B200_TC_SINGLE", "1")
+    B, Hq, Hkv, D, BS = 2, 8, 2, 128, 16
+    ctx = [300, 260]
+    gen = torch.Generator().manual_seed(91)
+    nblk = [-(-c // BS) for c in ctx]
+    NB = sum(nblk) + 3
+    perm = torch.randperm(NB, generator=gen).to(torch.int32)
+    bt = torch.zeros(B, max(nblk), dtype=torch.int32)
+    K = torch.randn(NB, BS, Hkv, D, generator=gen) * 0.1
+    V = torch.randn(NB, BS, Hkv, D, generator=gen)
+    cur = 0
+    for b, n in enumerate(nblk):
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+        for i in range(n):
+            pos = i * BS + torch.arange(BS)
+            comp = torch.where(pos % 128 < 64, -40.0, 30.0)
+            comp = torch.where((pos >= 128) & (pos % 128 >= 64), 45.0, comp)
+            K[bt[b, i].long(), :, :, 0] = comp[:, None]
+    K = K.half()
+    V = V.half()
+    maxq = max(ctx)
+    Q = torch.randn(B, Hq, maxq, D, generator=gen) * 0.1
+    Q[..., 0] = 16.0
+    Q = Q.half()
+    q_len = torch.tensor(ctx, dtype=torch.int32)
+    kv_len = torch.tensor(ctx, dtype=torch.int32)
+    nb = torch.tensor(nblk, dtype=torch.int32)
+    O, L = fa.flash_attention_forward(Q.cuda(), K.cuda(), V.cuda(), q_len.cuda(), bt.cuda(), nb.cuda(), BS,
+                                      kv_len.cuda(), None, None, mode="prefill")
+    torch.cuda.synchronize()
+    O_or, L_or = orc.paged_attention(Q.float().numpy(), K.float().numpy(), V.float().numpy(), q_len.numpy(),
+                                     bt.numpy(), nb.numpy(), BS, kv_len.numpy(), None, None)
+    _compare(O, L, O_or, L_or, q_len.numpy(), TOL_F16, f"extreme logits {kernel}")
+
+
 def test_repeated_decode_calls_share_one_workspace(fa):
     """Alternating batch shapes (different grid chunking) through one
     workspace, three rounds: every call must match the oracle."""
