@@ -110,6 +110,13 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
+// Two fp16 base-2 exponentials in one MUFU.EX2 (packed f16x2 in and out);
+// ex2(-inf) == +0.
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));

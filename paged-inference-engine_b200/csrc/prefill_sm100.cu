@@ -736,6 +736,27 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         const int h = q >> 1;
         const uint32_t* rr = (h ? r1 : r0) + 16 * (q & 1);
         uint32_t pk[8];
+        if constexpr (!MMA_BF16) {
+          // fp16 P straight from MUFU: x = s*c - m rounded to fp16 (|x| <= 2^8,
+          // masked keys -inf -> P = 0), two exponentials per instruction.  The
+          // row sum adds the same fp16 values pairwise in fp16 (one rounding,
+          // relative 2^-12) and accumulates in fp32.
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                             f2_pack(neg_m, neg_m)),
+                      x0, x1);
+            pk[i] = ex2_h2(pack_f16(x0, x1));
+            if (i & 1) {
+              const float2 fs = __half22float2(
+                  __hadd2(*reinterpret_cast<const __half2*>(&pk[i - 1]), *reinterpret_cast<const __half2*>(&pk[i])));
+              lsum2[0] = f2_add(lsum2[0], f2_pack(fs.x, fs.y));
+            }
+          }
+          tmem_st8(trow + scol + 32 * hf + 8 * q, pk);
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float p0, p1;
