@@ -184,6 +184,23 @@ int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
                       size_t workspace_bytes, int32_t* status, void* stream);
 
 /*
+ * The two launches of paged_attn_decode as separate calls, for a caller that
+ * schedules them itself (other work between them, or its own stream order):
+ * paged_attn_decode_split runs the split-K kernel, which writes the final
+ * output of every (sequence, kv head) segment that one worker covered and
+ * leaves fp32 partials (running max, sum, unnormalised O) in `workspace` for
+ * the others; paged_attn_reduce then combines those partials into O and LSE
+ * (the paged_attn_reduce step of the flash-decoding split; the reference's
+ * single kernel, kernels/flash_attention.py:19-136, has no separate reduce).
+ * Both calls take the same arguments and the same workspace, and the reduce
+ * must run after the split on the same stream (or after an event of it).
+ */
+int paged_attn_decode_split(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                            size_t workspace_bytes, int32_t* status, void* stream);
+int paged_attn_reduce(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
  * paged_attn_decode without a caller-supplied workspace.  It has no
  * counterpart in the reference.  It is meant for callers that cannot allocate
  * device memory per call: a serving engine that has pre-reserved all of HBM for

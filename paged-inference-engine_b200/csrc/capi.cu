@@ -261,7 +261,8 @@ WsLayout ws_layout(int warps, int D, int B) {
   return l;
 }
 
-int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream) {
+int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream,
+               int phase = pa::DECODE_BOTH) {
   if (p.B > kMaxDecodeSeqs)
     return fail(PA_ERR_UNSUPPORTED, "decode kernel supports at most %d sequences per call", kMaxDecodeSeqs);
   if (p.maxq * p.G > kNcMax)
@@ -285,7 +286,7 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
   p.tstart = reinterpret_cast<int*>(base + L.tstart);
   p.num_warps_total = warps;
   cudaError_t e = pa::launch_decode(p, tma ? &maps : nullptr, kv_k, p.q_bf16, kv->head_dim, nt, plan,
-                                    static_cast<cudaStream_t>(stream));
+                                    static_cast<cudaStream_t>(stream), phase);
   if (e != cudaSuccess) return cuda_fail(e, "decode launch");
   return PA_OK;
 }
@@ -464,6 +465,24 @@ int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
   return run_decode(p, kv, workspace, workspace_bytes, stream);
+}
+
+int paged_attn_decode_split(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                            size_t workspace_bytes, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  return run_decode(p, kv, workspace, workspace_bytes, stream, pa::DECODE_SPLIT);
+}
+
+int paged_attn_reduce(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                      size_t workspace_bytes, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  return run_decode(p, kv, workspace, workspace_bytes, stream, pa::DECODE_MERGE);
 }
 
 int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,

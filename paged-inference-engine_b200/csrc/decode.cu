@@ -971,14 +971,19 @@ struct DecodeInst {
     out->ctas = sms * per_sm;
     return 0;
   }
-  static cudaError_t launch(const AttnParams& p, const KvMaps& maps, const DecodeLaunch& pl, cudaStream_t stream) {
-    auto kern = pa_decode_kernel<D, KVT, QT, NT, TMA>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
-    if (e != cudaSuccess) return e;
-    e = launch_pdl(kern, dim3(pl.ctas), dim3(pl.warps_per_cta * 32), pl.smem, stream, p, maps);
-    if (e != cudaSuccess) return e;
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+  static cudaError_t launch(const AttnParams& p, const KvMaps& maps, const DecodeLaunch& pl, int phase,
+                            cudaStream_t stream) {
+    cudaError_t e;
+    if (phase != DECODE_MERGE) {
+      auto kern = pa_decode_kernel<D, KVT, QT, NT, TMA>;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem));
+      if (e != cudaSuccess) return e;
+      e = launch_pdl(kern, dim3(pl.ctas), dim3(pl.warps_per_cta * 32), pl.smem, stream, p, maps);
+      if (e != cudaSuccess) return e;
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      if (phase == DECODE_SPLIT) return cudaSuccess;
+    }
     e = launch_pdl(pa_decode_merge_kernel<D>, dim3(p.Hkv, p.B), dim3(128), 0, stream, p);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
@@ -991,11 +996,13 @@ struct Sel {
     if (nt == 1) return tma ? DecodeInst<D, KVT, QT, 1, true>::plan(B, o) : DecodeInst<D, KVT, QT, 1, false>::plan(B, o);
     return tma ? DecodeInst<D, KVT, QT, 2, true>::plan(B, o) : DecodeInst<D, KVT, QT, 2, false>::plan(B, o);
   }
-  static cudaError_t launch(const AttnParams& p, const KvMaps& m, int nt, bool tma, const DecodeLaunch& pl,
+  static cudaError_t launch(const AttnParams& p, const KvMaps& m, int nt, bool tma, const DecodeLaunch& pl, int ph,
                             cudaStream_t s) {
     if (nt == 1)
-      return tma ? DecodeInst<D, KVT, QT, 1, true>::launch(p, m, pl, s) : DecodeInst<D, KVT, QT, 1, false>::launch(p, m, pl, s);
-    return tma ? DecodeInst<D, KVT, QT, 2, true>::launch(p, m, pl, s) : DecodeInst<D, KVT, QT, 2, false>::launch(p, m, pl, s);
+      return tma ? DecodeInst<D, KVT, QT, 1, true>::launch(p, m, pl, ph, s)
+                 : DecodeInst<D, KVT, QT, 1, false>::launch(p, m, pl, ph, s);
+    return tma ? DecodeInst<D, KVT, QT, 2, true>::launch(p, m, pl, ph, s)
+               : DecodeInst<D, KVT, QT, 2, false>::launch(p, m, pl, ph, s);
   }
 };
 
@@ -1007,12 +1014,17 @@ int plan_kv(int kv, int qbf, int nt, int B, bool tma, DecodeLaunch* o) {
 }
 template <int D>
 cudaError_t launch_kv(const AttnParams& p, const KvMaps& m, int kv, int qbf, int nt, bool tma, const DecodeLaunch& pl,
-                      cudaStream_t s) {
+                      int ph, cudaStream_t s) {
+  if (ph == DECODE_MERGE)  // the merge kernel depends on head_dim only
+    return Sel<D, KV_F16, Q_F16>::launch(p, m, nt, tma, pl, ph, s);
   if (kv == KV_F16)
-    return qbf ? Sel<D, KV_F16, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_F16, Q_F16>::launch(p, m, nt, tma, pl, s);
+    return qbf ? Sel<D, KV_F16, Q_BF16>::launch(p, m, nt, tma, pl, ph, s)
+               : Sel<D, KV_F16, Q_F16>::launch(p, m, nt, tma, pl, ph, s);
   if (kv == KV_BF16)
-    return qbf ? Sel<D, KV_BF16, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_BF16, Q_F16>::launch(p, m, nt, tma, pl, s);
-  return qbf ? Sel<D, KV_I8, Q_BF16>::launch(p, m, nt, tma, pl, s) : Sel<D, KV_I8, Q_F16>::launch(p, m, nt, tma, pl, s);
+    return qbf ? Sel<D, KV_BF16, Q_BF16>::launch(p, m, nt, tma, pl, ph, s)
+               : Sel<D, KV_BF16, Q_F16>::launch(p, m, nt, tma, pl, ph, s);
+  return qbf ? Sel<D, KV_I8, Q_BF16>::launch(p, m, nt, tma, pl, ph, s)
+             : Sel<D, KV_I8, Q_F16>::launch(p, m, nt, tma, pl, ph, s);
 }
 
 }  // namespace
@@ -1024,12 +1036,12 @@ int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, Deco
 }
 
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
-                          const DecodeLaunch& plan, cudaStream_t stream) {
+                          const DecodeLaunch& plan, cudaStream_t stream, int phase) {
   KvMaps none{};
   const KvMaps& m = maps ? *maps : none;
   const bool tma = maps != nullptr;
-  if (D == 64) return launch_kv<64>(p, m, kv_kind, q_bf16, nt, tma, plan, stream);
-  if (D == 128) return launch_kv<128>(p, m, kv_kind, q_bf16, nt, tma, plan, stream);
+  if (D == 64) return launch_kv<64>(p, m, kv_kind, q_bf16, nt, tma, plan, phase, stream);
+  if (D == 128) return launch_kv<128>(p, m, kv_kind, q_bf16, nt, tma, plan, phase, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -107,8 +107,12 @@ struct DecodeLaunch {
 };
 // use_tma: the pool can be read with TMA boxes (block_size >= 8, maps built).
 int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, DecodeLaunch* out);
+// phase: DECODE_BOTH launches the split kernel and the merge kernel,
+// DECODE_SPLIT only the split kernel, DECODE_MERGE only the merge kernel (over
+// the workspace a DECODE_SPLIT launch with the same problem filled).
+enum : int { DECODE_BOTH = 0, DECODE_SPLIT = 1, DECODE_MERGE = 2 };
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
-                          const DecodeLaunch& plan, cudaStream_t stream);
+                          const DecodeLaunch& plan, cudaStream_t stream, int phase = DECODE_BOTH);
 cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);
 // tcgen05/TMEM prefill (16-bit pools, head_dim 128, block_size >= 8).
 bool prefill_tc_supported(int kv_kind, int D, int BS);
