@@ -222,6 +222,25 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
                               int32_t* status, void* stream);
 
 /*
+ * paged_attn_forward over ragged query rows, for callers that keep the rows of
+ * all sequences packed instead of padding them to max_q_len (the pad / unpad
+ * loops of transformer/model.py:133-141,162-167 and the padded Q of
+ * kernels/flash_attention.py:139-150):
+ *   q_start       int32 [num_seqs] on the device, first row of each sequence
+ *                 (cu_seqlens[:-1]); sequence b owns rows q_start[b] ..
+ *                 q_start[b] + q_len_per_seq[b] - 1
+ *   total_q_rows  T, the rows of Q / O / L
+ * io->q is [T, num_q_heads, head_dim] (io->q_stride_row between rows,
+ * io->q_stride_head between heads; q_stride_seq is unused), O likewise and
+ * LSE [T, num_q_heads]; io->max_q_len >= every q_len_per_seq[b] sizes the
+ * grid.  Rows outside [0, T) are never read or written: a sequence's rows
+ * are clamped to T - q_start[b].  Picks the decode or prefill kernel as
+ * paged_attn_forward does; the workspace rule is the same.
+ */
+int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, const int32_t* q_start,
+                      int32_t total_q_rows, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
  * Tiled causal paged attention for long query blocks (prefill / chunked
  * prefill): the q_len > 1 grid of kernels/flash_attention.py:19-136.
  */

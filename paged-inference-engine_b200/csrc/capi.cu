@@ -293,12 +293,16 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
 
 // 4-D TMA map over Q [num_seqs, num_q_heads, max_q_len, 128] (d contiguous):
 // box = 64 columns x 128 rows, 128-byte swizzle; rows past max_q_len read as zeros.
-bool make_q_map(CUtensorMap* m, const pa_attn_io_t* io, int D, int B) {
+// Ragged rows (q_total > 0): Q packed as [q_total, num_q_heads, 128], mapped as
+// [1, num_q_heads, q_total, 128]; rows past q_total read as zeros.
+bool make_q_map(CUtensorMap* m, const pa_attn_io_t* io, int D, int B, int q_total = 0) {
   auto enc = encode_fn();
   if (!enc || D != 128) return false;
-  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(io->max_q_len),
-                              static_cast<cuuint64_t>(io->num_q_heads), static_cast<cuuint64_t>(B)};
-  const long long st[3] = {io->q_stride_row, io->q_stride_head, io->q_stride_seq};
+  const bool ragged = q_total > 0;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(ragged ? q_total : io->max_q_len),
+                              static_cast<cuuint64_t>(io->num_q_heads), static_cast<cuuint64_t>(ragged ? 1 : B)};
+  const long long st[3] = {io->q_stride_row, io->q_stride_head,
+                           ragged ? io->q_stride_row * static_cast<long long>(q_total) : io->q_stride_seq};
   for (long long x : st)
     if (x <= 0) return false;
   const cuuint64_t strides[3] = {static_cast<cuuint64_t>(st[0] * 2), static_cast<cuuint64_t>(st[1] * 2),
@@ -319,7 +323,7 @@ int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, const pa_attn_io_t* 
       row_al(io->o_stride_row, 2, 16)) {
     pa::KvMaps maps;
     CUtensorMap qmap;
-    if (make_kv_maps(kv, &maps) && make_q_map(&qmap, io, kv->head_dim, p.B)) {
+    if (make_kv_maps(kv, &maps) && make_q_map(&qmap, io, kv->head_dim, p.B, p.q_start ? p.q_total : 0)) {
       cudaError_t e = pa::launch_prefill_tc(p, maps.k, maps.v, qmap, kvk, static_cast<cudaStream_t>(stream));
       if (e != cudaSuccess) return cuda_fail(e, "prefill (tcgen05) launch");
       return PA_OK;
@@ -483,6 +487,21 @@ int paged_attn_reduce(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
   return run_decode(p, kv, workspace, workspace_bytes, stream, pa::DECODE_MERGE);
+}
+
+int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, const int32_t* q_start,
+                      int32_t total_q_rows, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  if (!q_start) return fail(PA_ERR_INVALID, "q_start is NULL");
+  if (total_q_rows < 0) return fail(PA_ERR_INVALID, "total_q_rows < 0");
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  if (total_q_rows == 0) return PA_OK;
+  p.q_start = q_start;
+  p.q_total = total_q_rows;
+  if (use_decode(p)) return run_decode(p, kv, workspace, workspace_bytes, stream);
+  return run_prefill(p, kv, io, stream);
 }
 
 int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,

@@ -117,7 +117,7 @@ template <int TK>
 __device__ __forceinline__ unsigned tile_rows() { return TK == 32 ? 0xffffffffu : ((1u << TK) - 1u); }
 
 // Query rows of sequence b, never more than the rows Q holds.
-__device__ __forceinline__ int seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
+__device__ __forceinline__ int seq_qlen(const AttnParams& p, int b) { return seq_rows(p, b); }
 
 __device__ __forceinline__ int seq_keys(const AttnParams& p, int b) {
   const int q = seq_qlen(p, b);
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
         const int qi = col / p.G;
         const int hq = col - qi * p.G;
         const bool valid = qi < qlen_b;
-        const unsigned short* qrow = static_cast<const unsigned short*>(p.q) + cp.b * p.q_sb +
+        const unsigned short* qrow = static_cast<const unsigned short*>(p.q) + q_seq_base(p, cp.b) +
                                      (cp.kvh * p.G + hq) * p.q_sh + static_cast<long long>(qi) * p.q_sm;
         if constexpr (!INT8) {
 #pragma unroll
@@ -840,7 +840,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
           if (complete) {
             const float inv = lt > 0.f ? 1.f / lt : 0.f;
             if (valid) {
-              __half* orow = static_cast<__half*>(p.o) + cp.b * p.o_sb + (cp.kvh * p.G + hq) * p.o_sh +
+              __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, cp.b) + (cp.kvh * p.G + hq) * p.o_sh +
                              static_cast<long long>(qi) * p.o_sm;
 #pragma unroll
               for (int mt = 0; mt < KS; ++mt)
@@ -851,7 +851,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
                 }
               if (r == 0 && p.lse) {
                 const float L = lt > 0.f ? (m_run[nt][e] + lg2(lt)) * 0.6931471805599453f : -INFINITY;
-                static_cast<__half*>(p.lse)[cp.b * p.l_sb + (cp.kvh * p.G + hq) * p.l_sh +
+                static_cast<__half*>(p.lse)[l_seq_base(p, cp.b) + (cp.kvh * p.G + hq) * p.l_sh +
                                             static_cast<long long>(qi) * p.l_sm] = __float2half_rn(L);
               }
             }
@@ -896,11 +896,11 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
     // no visible keys: O = 0, L = -inf
     for (int col = warp; col < ncols; col += 4) {
       const int qi = col / p.G, hq = col - (col / p.G) * p.G;
-      __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + (kvh * p.G + hq) * p.o_sh +
+      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh +
                      static_cast<long long>(qi) * p.o_sm;
       for (int d = lane; d < D; d += 32) orow[d] = __float2half_rn(0.f);
       if (lane == 0 && p.lse)
-        static_cast<__half*>(p.lse)[b * p.l_sb + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
+        static_cast<__half*>(p.lse)[l_seq_base(p, b) + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
             __float2half_rn(-INFINITY);
     }
     return;
@@ -935,13 +935,13 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
       for (int k = 0; k < D / 32; ++k) o[k] += po[lane + 32 * k] * f;
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + (kvh * p.G + hq) * p.o_sh +
+    __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh +
                    static_cast<long long>(qi) * p.o_sm;
 #pragma unroll
     for (int k = 0; k < D / 32; ++k) orow[lane + 32 * k] = __float2half_rn(o[k] * inv);
     if (lane == 0 && p.lse) {
       const float L = l > 0.f ? (M + lg2(l)) * 0.6931471805599453f : -INFINITY;
-      static_cast<__half*>(p.lse)[b * p.l_sb + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
+      static_cast<__half*>(p.lse)[l_seq_base(p, b) + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
           __float2half_rn(L);
     }
   }

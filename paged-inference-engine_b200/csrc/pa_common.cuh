@@ -110,17 +110,33 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
-// Two fp16 base-2 exponentials in one MUFU.EX2 (packed f16x2 in and out);
-// ex2(-inf) == +0.
-__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;\n" : "=r"(y) : "r"(x));
-  return y;
-}
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Row bases of sequence b in Q, O and L: b * seq_stride for [B, H, maxq, ...]
+// tensors, q_start[b] * row_stride for ragged rows packed as [T, H, ...].
+__device__ __forceinline__ long long q_seq_base(const AttnParams& p, int b) {
+  return p.q_start ? static_cast<long long>(p.q_start[b]) * p.q_sm : static_cast<long long>(b) * p.q_sb;
+}
+__device__ __forceinline__ long long o_seq_base(const AttnParams& p, int b) {
+  return p.q_start ? static_cast<long long>(p.q_start[b]) * p.o_sm : static_cast<long long>(b) * p.o_sb;
+}
+__device__ __forceinline__ long long l_seq_base(const AttnParams& p, int b) {
+  return p.q_start ? static_cast<long long>(p.q_start[b]) * p.l_sm : static_cast<long long>(b) * p.l_sb;
+}
+// Query rows of sequence b: q_len clamped to max_q_len and, for ragged rows,
+// to the rows left in Q after q_start[b] (0 for a start outside [0, T)), so
+// bad metadata can never address past Q, O or L.
+__device__ __forceinline__ int seq_rows(const AttnParams& p, int b) {
+  int q = min(p.qlen[b], p.maxq);
+  if (p.q_start) {
+    const int s = p.q_start[b];
+    q = (s < 0 || s >= p.q_total) ? 0 : min(q, p.q_total - s);
+  }
+  return q;
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

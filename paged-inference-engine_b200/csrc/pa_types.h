@@ -34,6 +34,11 @@ struct AttnParams {
   const void* q;
   long long q_sb, q_sh, q_sm;
   int q_bf16;
+  // Ragged rows: when q_start is set, sequence b's rows start at row
+  // q_start[b] of Q, O and L, which are packed as [T, Hq, D] / [T, Hq]
+  // (q_total = T rows; the per-sequence strides are unused).
+  const int* q_start;
+  int q_total;
   // KV pool, logical [block, slot, head, d]
   const void* k;
   const void* v;

@@ -23,7 +23,7 @@ constexpr int PF_BM = 64;
 constexpr int PF_BN = 64;
 constexpr int PF_THREADS = 128;
 
-__device__ __forceinline__ int pf_seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
+__device__ __forceinline__ int pf_seq_qlen(const AttnParams& p, int b) { return seq_rows(p, b); }
 
 __device__ __forceinline__ int pf_seq_keys(const AttnParams& p, int b) {
   const int q = pf_seq_qlen(p, b);
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(PF_THREADS) pa_prefill_kernel(const AttnParams
 
   // ---- Q tile ---------------------------------------------------------------
   {
-    const unsigned short* qbase = static_cast<const unsigned short*>(p.q) + b * p.q_sb + hq * p.q_sh;
+    const unsigned short* qbase = static_cast<const unsigned short*>(p.q) + q_seq_base(p, b) + hq * p.q_sh;
 #pragma unroll
     for (int it = 0; it < PF_BM * C::CH / PF_THREADS; ++it) {
       const int c = it * PF_THREADS + tid;
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(PF_THREADS) pa_prefill_kernel(const AttnParams
     lt[h] += __shfl_xor_sync(0xffffffffu, lt[h], 1);
     lt[h] += __shfl_xor_sync(0xffffffffu, lt[h], 2);
   }
-  __half* obase = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh;
+  __half* obase = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int qi = h ? qi_b : qi_a;
@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(PF_THREADS) pa_prefill_kernel(const AttnParams
     }
     if (q4 == 0 && p.lse) {
       const float L = lt[h] > 0.f ? (m_run[h] + lg2(lt[h])) * 0.6931471805599453f : -INFINITY;
-      static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
+      static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
           __float2half_rn(L);
     }
   }

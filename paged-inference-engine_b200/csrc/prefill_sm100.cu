@@ -66,7 +66,7 @@ struct alignas(64) TcMaps {
   CUtensorMap q;
 };
 
-__device__ __forceinline__ int tc_seq_qlen(const AttnParams& p, int b) { return min(p.qlen[b], p.maxq); }
+__device__ __forceinline__ int tc_seq_qlen(const AttnParams& p, int b) { return seq_rows(p, b); }
 
 __device__ __forceinline__ int tc_seq_keys(const AttnParams& p, int b, int q) {
   if (q <= 0) return 0;
@@ -178,8 +178,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0 && nt > 0) {
       mbar_arrive_expect_tx(bar(E_QFULL), TILE_B);
-      tma_load_4d(base, &maps.q, bar(E_QFULL), 0, m0, hq, b);
-      tma_load_4d(base + HALF_B, &maps.q, bar(E_QFULL), 64, m0, hq, b);
+      // Q tile: rows m0.. of sequence b (ragged rows: rows q_start[b] + m0.. of the packed Q; rows past
+      // its end read as zeros and rows of the next sequence are computed but never stored)
+      const int q_row0 = p.q_start ? p.q_start[b] + m0 : m0;
+      const int q_seq = p.q_start ? 0 : b;
+      tma_load_4d(base, &maps.q, bar(E_QFULL), 0, q_row0, hq, q_seq);
+      tma_load_4d(base + HALF_B, &maps.q, bar(E_QFULL), 64, q_row0, hq, q_seq);
     }
     if (nt > 0) {
       // Lane i owns box i of every tile: the block ids of a tile are fetched in
@@ -415,7 +419,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     named_barrier_sync(2, 256);
     const float lt = l + mxs[(hf ^ 1) * 128 + r];
     const bool valid = row < qlen;
-    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
+    __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
                    64 * hf;
     if (nt > 0) {
       wait_o_done(nt - 1);
@@ -443,7 +447,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (valid && p.lse && hf == 0) {
       const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
-      static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+      static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
           __float2half_rn(L);
     }
   }
@@ -550,10 +554,14 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0 && nt > 0) {
       mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
+      // Q tile: rows m0.. of sequence b (ragged rows: rows q_start[b] + m0.. of the packed Q; rows past
+      // its end read as zeros and rows of the next sequence are computed but never stored)
+      const int q_row0 = p.q_start ? p.q_start[b] + m0 : m0;
+      const int q_seq = p.q_start ? 0 : b;
 #pragma unroll
       for (int x = 0; x < 2; ++x) {
-        tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, m0, hq0 + x, b);
-        tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, m0, hq0 + x, b);
+        tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, q_row0, hq0 + x, q_seq);
+        tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, q_row0, hq0 + x, q_seq);
       }
     }
     if (nt > 0) {
@@ -736,27 +744,6 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         const int h = q >> 1;
         const uint32_t* rr = (h ? r1 : r0) + 16 * (q & 1);
         uint32_t pk[8];
-        if constexpr (!MMA_BF16) {
-          // fp16 P straight from MUFU: x = s*c - m rounded to fp16 (|x| <= 2^8,
-          // masked keys -inf -> P = 0), two exponentials per instruction.  The
-          // row sum adds the same fp16 values pairwise in fp16 (one rounding,
-          // relative 2^-12) and accumulates in fp32.
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
-                             f2_pack(neg_m, neg_m)),
-                      x0, x1);
-            pk[i] = ex2_h2(pack_f16(x0, x1));
-            if (i & 1) {
-              const float2 fs = __half22float2(
-                  __hadd2(*reinterpret_cast<const __half2*>(&pk[i - 1]), *reinterpret_cast<const __half2*>(&pk[i])));
-              lsum2[0] = f2_add(lsum2[0], f2_pack(fs.x, fs.y));
-            }
-          }
-          tmem_st8(trow + scol + 32 * hf + 8 * q, pk);
-          continue;
-        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float p0, p1;
@@ -819,7 +806,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     const float lt = combine(l, false);
     const int hq = hq0 + x;
     const bool valid = row < qlen;
-    __half* orow = static_cast<__half*>(p.o) + b * p.o_sb + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
+    __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
                    64 * hf;
     if (nt > 0) {
       wait_or_flag(p, bar(C_ODONE + x), (nt - 1) & 1);  // the last P*V (phase nt-1)
@@ -847,7 +834,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     }
     if (valid && p.lse && hf == 0) {
       const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
-      static_cast<__half*>(p.lse)[b * p.l_sb + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+      static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
           __float2half_rn(L);
     }
   }

@@ -45,7 +45,7 @@ if _PKG_ROOT not in sys.path:
 
 from pie_b200 import ops as _ops  # noqa: E402
 
-__all__ = ["flash_attention_forward", "FlashAttentionFunction", "write_kv_cache"]
+__all__ = ["flash_attention_forward", "flash_attention_varlen", "FlashAttentionFunction", "write_kv_cache"]
 
 
 def flash_attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per_seq, block_table,
@@ -62,6 +62,24 @@ def flash_attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q
     return _ops.paged_attention(Q, K, V, q_len_per_seq, block_table, num_blocks_per_seq, int(block_size),
                                 kv_len_per_seq, k_scale_ptr, v_scale_ptr, out=out, lse=lse,
                                 causal_top_left=causal_top_left, softmax_scale=softmax_scale, mode=mode)
+
+
+def flash_attention_varlen(q, cu_seqlens_q, K, V, block_table, num_blocks_per_seq, block_size, kv_len_per_seq,
+                           k_scale_ptr=None, v_scale_ptr=None, *, max_q_len=None, out=None, lse=None,
+                           causal_top_left: bool = False, softmax_scale=None):
+    """flash_attention_forward over packed query rows; returns (O, L) float16.
+
+    ``q`` is ``[T, H, D]`` holding the rows of every sequence back to back,
+    sequence b at rows ``cu_seqlens_q[b] : cu_seqlens_q[b + 1]`` (int32 on the
+    device), so the caller builds no padded ``[B, H, max_q_len, D]`` copy and
+    reads no padded output back (transformer/model.py:133-141,162-167).  O is
+    ``[T, H, D]``, L ``[T, H]``.  Pass ``max_q_len`` to avoid the one host read
+    of ``cu_seqlens_q``.
+    """
+    assert q.is_cuda and K.is_cuda and V.is_cuda, "Not CUDA Tensors -_-"
+    return _ops.paged_attention_varlen(q, cu_seqlens_q, K, V, block_table, num_blocks_per_seq, int(block_size),
+                                       kv_len_per_seq, k_scale_ptr, v_scale_ptr, max_q_len=max_q_len, out=out,
+                                       lse=lse, causal_top_left=causal_top_left, softmax_scale=softmax_scale)
 
 
 class FlashAttentionFunction(torch.autograd.Function):

@@ -93,6 +93,9 @@ SIGNATURES = {
                                                ctypes.POINTER(PaPaging), _vp, ctypes.c_size_t, _vp, _vp]),
     "paged_attn_reduce": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
                                          ctypes.POINTER(PaPaging), _vp, ctypes.c_size_t, _vp, _vp]),
+    "paged_attn_varlen": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
+                                         ctypes.POINTER(PaPaging), _vp, ctypes.c_int32, _vp, ctypes.c_size_t,
+                                         _vp, _vp]),
     "paged_attn_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
                                                  ctypes.POINTER(PaPaging), _vp, _vp]),
     "paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),

@@ -216,6 +216,82 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
     return out, lse
 
 
+def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
+                           block_table: torch.Tensor, num_blocks_per_seq: torch.Tensor, block_size: int,
+                           kv_len_per_seq: torch.Tensor, k_scale: Optional[torch.Tensor] = None,
+                           v_scale: Optional[torch.Tensor] = None, *, max_q_len: Optional[int] = None,
+                           out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                           causal_top_left: bool = False, softmax_scale: Optional[float] = None,
+                           status: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Paged causal attention over ragged query rows through paged_attn_varlen.
+
+    Q is ``[T, Hq, D]`` with the rows of sequence b at
+    ``cu_seqlens_q[b] : cu_seqlens_q[b + 1]``; returns O ``[T, Hq, D]`` and L
+    ``[T, Hq]`` (fp16).  ``max_q_len`` (the longest sequence's row count) sizes
+    the grid; without it one host read of ``cu_seqlens_q`` finds it.
+    """
+    if Q.dim() != 3:
+        raise ValueError("Q must be [total_q_rows, num_q_heads, head_dim]")
+    T, Hq, D = Q.shape
+    B = block_table.shape[0]
+    if cu_seqlens_q.dim() != 1 or cu_seqlens_q.shape[0] != B + 1:
+        raise ValueError(f"cu_seqlens_q must hold {B + 1} offsets for {B} sequences")
+    if K.shape[1] != block_size:
+        raise ValueError(f"block_size {block_size} does not match the pool's slot dimension {K.shape[1]}")
+    if K.shape[3] != D:
+        raise ValueError(f"head_dim of Q ({D}) and of the pool ({K.shape[3]}) differ")
+    dev = Q.device
+    for name, t in (("K", K), ("V", V), ("block_table", block_table), ("cu_seqlens_q", cu_seqlens_q),
+                    ("kv_len_per_seq", kv_len_per_seq), ("num_blocks_per_seq", num_blocks_per_seq)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, Q on {dev}")
+    cu = _i32(cu_seqlens_q)
+    q_start = cu[:-1]
+    q_len = (cu[1:] - cu[:-1]).contiguous()
+    if max_q_len is None:
+        max_q_len = int(q_len.max().item()) if B else 0
+    mma_dtype = K.dtype if K.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    if Q.dtype not in (torch.float16, torch.bfloat16):
+        Q = Q.to(mma_dtype)
+    if Q.stride(2) != 1:
+        Q = Q.contiguous()
+    keep: list = [cu, q_len]
+    kc = kv_cache_desc(K, V, k_scale, v_scale)
+    pg = paging_desc(block_table, num_blocks_per_seq, q_len, kv_len_per_seq, keep)
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.float16, device=dev)
+    elif out.dtype != torch.float16 or tuple(out.shape) != (T, Hq, D):
+        raise ValueError("out must be float16 with Q's shape")
+    if lse is None:
+        lse = torch.empty((T, Hq), dtype=torch.float16, device=dev)
+    io = PaAttnIO()
+    io.q = Q.data_ptr()
+    io.q_dtype = _TORCH2PA[Q.dtype]
+    io.num_q_heads, io.max_q_len = Hq, int(max_q_len)
+    io.causal_top_left = 1 if causal_top_left else 0
+    io.q_stride_seq, io.q_stride_head, io.q_stride_row = 0, Q.stride(1), Q.stride(0)
+    io.o = out.data_ptr()
+    io.o_stride_seq, io.o_stride_head, io.o_stride_row = 0, out.stride(1), out.stride(0)
+    io.lse = lse.data_ptr()
+    io.l_stride_seq, io.l_stride_head, io.l_stride_row = 0, lse.stride(1), lse.stride(0)
+    io.softmax_scale = float(softmax_scale) if softmax_scale else 0.0
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if status is None and _CHECK:
+        status = status_word(dev)
+    st_ptr = _ptr(status)
+    with torch.cuda.device(dev):
+        nbytes = ctypes.c_size_t(0)
+        _lib.check("paged_attn_workspace_size", lib.paged_attn_workspace_size(io, kc, pg, ctypes.byref(nbytes)))
+        ws = workspace(dev, nbytes.value) if nbytes.value else None
+        _lib.check("paged_attn_varlen", lib.paged_attn_varlen(io, kc, pg, q_start.data_ptr(), T, _ptr(ws),
+                                                              0 if ws is None else ws.numel(), st_ptr, stream))
+    if _CHECK and status is not None:
+        _raise_status("paged_attention_varlen", status)
+    return out, lse
+
+
 def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor, seq_index: torch.Tensor,
              positions: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
              k_scale: Optional[torch.Tensor] = None, v_scale: Optional[torch.Tensor] = None, *,
