@@ -24,6 +24,9 @@
 #ifndef PA_WRITE_MINB
 #define PA_WRITE_MINB 4
 #endif
+#ifndef PA_WRITE_THREADS
+#define PA_WRITE_THREADS 256
+#endif
 
 namespace pa {
 namespace {
@@ -104,6 +107,24 @@ __device__ __forceinline__ uint32_t pack_bytes(uint32_t b0, uint32_t b1, uint32_
   return prmt(prmt(b0, b1, 0x0040u), prmt(b2, b3, 0x0040u), 0x5410u);
 }
 
+// max |x| over one 16-byte load, from the packed values: |x| and max are
+// exact in 16 bits, so this equals the fp32 maximum of the unpacked row.
+template <int IN>
+__device__ __forceinline__ float load_absmax(const uint4& w) {
+  if constexpr (IN == PA_DTYPE_F32) {
+    return fmaxf(fmaxf(fabsf(__uint_as_float(w.x)), fabsf(__uint_as_float(w.y))),
+                 fmaxf(fabsf(__uint_as_float(w.z)), fabsf(__uint_as_float(w.w))));
+  } else if constexpr (IN == PA_DTYPE_BF16) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+    const __nv_bfloat162 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__bfloat162float(m.x), __bfloat162float(m.y));
+  } else {
+    const __half2* h = reinterpret_cast<const __half2*>(&w);
+    const __half2 m = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+    return fmaxf(__half2float(m.x), __half2float(m.y));
+  }
+}
+
 template <int EPL>
 __device__ __forceinline__ bool quant_row_fast(const float (&f)[EPL], float inv, uint32_t (&w)[EPL / 4]) {
   bool near = false;
@@ -137,7 +158,7 @@ __device__ __forceinline__ void quant_row_exact(const float (&f)[EPL], float s, 
 // heads): the group's K and V source rows are loaded before the token's
 // block-table entry is known, so the index lookups overlap the row loads.
 template <int IN, int D>
-__global__ void __launch_bounds__(256, PA_WRITE_MINB) kv_write_kernel(const WriteParams p) {
+__global__ void __launch_bounds__(PA_WRITE_THREADS, PA_WRITE_MINB) kv_write_kernel(const WriteParams p) {
   pdl_enter();
   using C = WCfg<IN, D>;
   constexpr int EPL = C::EPL;
@@ -189,16 +210,10 @@ __global__ void __launch_bounds__(256, PA_WRITE_MINB) kv_write_kernel(const Writ
   // The NL rows of a lane are independent: each phase runs over all of them
   // before the next, so their latencies overlap.
   if (p.cache_dtype == PA_DTYPE_I8) {
+    // rows stay packed; each is unpacked only while it is quantised
     float am[C::NL];
-    float fv[C::NL][EPL];
 #pragma unroll
-    for (int it = 0; it < C::NL; ++it) {
-      unpack_row<IN, EPL>(raw[it], fv[it]);
-      float a = 0.f;
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) a = fmaxf(a, fabsf(fv[it][i]));
-      am[it] = a;
-    }
+    for (int it = 0; it < C::NL; ++it) am[it] = load_absmax<IN>(raw[it]);
 #pragma unroll
     for (int o = C::LPR / 2; o >= 1; o >>= 1)
 #pragma unroll
@@ -209,12 +224,18 @@ __global__ void __launch_bounds__(256, PA_WRITE_MINB) kv_write_kernel(const Writ
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
       sc[it] = (am[it] == 0.f) ? 1.0f : div127_rn(am[it]);
-      if (quant_row_fast<EPL>(fv[it], rcp_approx(sc[it]), w[it])) near |= 1u << it;
+      float f[EPL];
+      unpack_row<IN, EPL>(raw[it], f);
+      if (quant_row_fast<EPL>(f, rcp_approx(sc[it]), w[it])) near |= 1u << it;
     }
     // rows with a quotient near a rounding boundary: redo with the division
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
-      if (__any_sync(0xffffffffu, (near >> it) & 1u)) quant_row_exact<EPL>(fv[it], sc[it], w[it]);
+      if (__any_sync(0xffffffffu, (near >> it) & 1u)) {
+        float f[EPL];
+        unpack_row<IN, EPL>(raw[it], f);
+        quant_row_exact<EPL>(f, sc[it], w[it]);
+      }
     }
 #pragma unroll
     for (int it = 0; it < C::NL; ++it) {
@@ -263,8 +284,8 @@ template <int IN>
 cudaError_t launch_in(const WriteParams& p, cudaStream_t stream) {
   auto go = [&](auto kern, int hg) {
     const long long warps = static_cast<long long>(p.T) * ((p.Hkv + hg - 1) / hg);
-    const long long blocks = (warps * 32 + 255) / 256;
-    return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p);
+    const long long blocks = (warps * 32 + PA_WRITE_THREADS - 1) / PA_WRITE_THREADS;
+    return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(PA_WRITE_THREADS), 0, stream, p);
   };
   if (p.D == 64) return go(kv_write_kernel<IN, 64>, WCfg<IN, 64>::HG);
   if (p.D == 128) return go(kv_write_kernel<IN, 128>, WCfg<IN, 128>::HG);
