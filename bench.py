@@ -362,9 +362,10 @@ class PrefillWorkload(Workload):
 class LongCtxWorkload(Workload):
     """long_ctx_int8: B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8; KV heads sharded over ranks."""
 
-    def __init__(self, ws: int, rank: int, device, cpu_only: bool = False):
+    def __init__(self, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl"):
         from pie_b200.workloads import CONFIGS, draw_context_lengths
 
+        self.exchange = exchange
         cfg = CONFIGS["long_ctx_int8"]
         self.cfg = cfg
         Bn, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
@@ -389,7 +390,7 @@ class LongCtxWorkload(Workload):
 
         c = self.cfg
         Bn, Hq, Hkv, D, BS = c["B"], c["Hq"], c["Hkv"], c["D"], c["BS"]
-        dec = KVHeadShardedDecoder(Hq, Hkv, D)
+        dec = KVHeadShardedDecoder(Hq, Hkv, D, exchange=self.exchange)
         K, V, ks, vs, bt, nblk, NB = build_rank_pool(self.ctx, Hkv // self.ws, D, BS, 1000 + self.rank, device)
         Qfull = torch.randn(Bn, Hq, 1, D, generator=torch.Generator().manual_seed(5)).half()
         Ql = dec.local_q(Qfull).contiguous().to(device)
@@ -436,11 +437,11 @@ class LongCtxWorkload(Workload):
         return f"{n} sequences (4 distinct, ctx from the workload's range, all 8 KV heads), {t:.1f} s"
 
 
-def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False) -> Workload:
+def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl") -> Workload:
     if name == "prefill_bf16":
         return PrefillWorkload(1000 + rank, device, cpu_only)
     if name == "long_ctx_int8":
-        return LongCtxWorkload(ws, rank, device, cpu_only)
+        return LongCtxWorkload(ws, rank, device, cpu_only, exchange)
     return DecodeWorkload(name, 1000 + rank, device, cpu_only)
 
 
@@ -494,6 +495,8 @@ def main():
                     choices=["decode_fp16", "decode_int8", "prefill_bf16", "long_ctx_int8"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="long_ctx_int8 head-output exchange: NCCL all-gather or stores into peer buffers")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -507,7 +510,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     peaks, peak_kind = load_peaks()
-    w = make_workload(a.workload, ws, rank, device)
+    w = make_workload(a.workload, ws, rank, device, exchange=a.exchange)
     if w.bound == "hbm":
         peak, punit = peaks["hbm_gbs"], "GB/s"
     else:
@@ -536,7 +539,9 @@ def main():
         "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
         "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
         "config": {"workload": a.workload, **w.info,
-                   "parallelism": (f"kv-head shard x{ws} + NCCL all_gather" if w.scaling == "strong"
+                   "parallelism": ((f"kv-head shard x{ws} + " +
+                                    ("NCCL all_gather" if getattr(w, "exchange", "nccl") == "nccl"
+                                     else "output rows stored into peer buffers")) if w.scaling == "strong"
                                    else f"dp{ws} (one batch per rank)"),
                    "l2": "inputs larger than L2 (126 MB)"},
         "roofline": {"bound": w.bound, "achieved": round(dom, 2), "peak": peak, "unit": punit,

@@ -62,7 +62,8 @@ enum {
   PA_STATUS_BAD_BLOCK_ID = 1,
   PA_STATUS_BAD_POSITION = 2,
   PA_STATUS_BAD_NUM_BLOCKS = 4,
-  PA_STATUS_BAD_SEQ_INDEX = 8
+  PA_STATUS_BAD_SEQ_INDEX = 8,
+  PA_STATUS_PEER_TIMEOUT = 32
 };
 
 /*
@@ -239,6 +240,42 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
  */
 int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, const int32_t* q_start,
                       int32_t total_q_rows, void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * Head-sharded decode with the output exchange fused into the attention
+ * kernels (the NCCL all-gather of head outputs that follows per-GPU decode in
+ * a KV-head-sharded engine; the reference runs on one GPU and has none).
+ * Each GPU of one box computes its KV heads and stores every finished O row
+ * straight into the output buffer of every GPU over NVLink, while its other
+ * heads are still being computed; paged_attn_peer_barrier then ends the step.
+ *
+ * Set-up, once per buffer and GPU (these allocate and map; the attention
+ * calls below never do):
+ *   paged_attn_peer_alloc   cudaMalloc + zero fill + a 64-byte IPC handle
+ *   paged_attn_peer_open    map another process's buffer from its handle
+ *   paged_attn_peer_close / paged_attn_peer_free
+ * Per step:
+ *   paged_attn_decode_peers  as paged_attn_decode, but O goes to o_peers[0..n)
+ *       (n <= 8): o_peers[r] points at the same logical position in GPU r's
+ *       buffer that io->o gives the layout for (the caller adds its own
+ *       head offset); LSE stays local.  Decode shapes only.
+ *   paged_attn_peer_barrier  posts `epoch` into slot `rank` of every peer's
+ *       int32 flag array and waits until every slot of local_flags holds
+ *       `epoch`: after it, this GPU's buffer holds every GPU's rows.  Each
+ *       wait gives up after about 0.4 s and sets PA_STATUS_PEER_TIMEOUT.
+ * Every GPU must make the same calls with the same epoch (increasing per
+ * step), and a buffer must not be written again while a peer still reads the
+ * previous step's rows (alternate two buffers).
+ */
+int paged_attn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int paged_attn_peer_free(void* ptr);
+int paged_attn_peer_open(const void* ipc_handle, void** ptr);
+int paged_attn_peer_close(void* ptr);
+int paged_attn_decode_peers(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                            size_t workspace_bytes, void* const* o_peers, int32_t n_peers, int32_t* status,
+                            void* stream);
+int paged_attn_peer_barrier(int32_t* local_flags, int32_t* const* peer_flags, int32_t n_peers, int32_t rank,
+                            int32_t epoch, int32_t* status, void* stream);
 
 /*
  * Tiled causal paged attention for long query blocks (prefill / chunked

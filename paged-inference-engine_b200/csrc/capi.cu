@@ -504,6 +504,80 @@ int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
   return run_prefill(p, kv, io, stream);
 }
 
+int paged_attn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  g_err[0] = 0;
+  if (!ptr || !ipc_handle || bytes == 0) return fail(PA_ERR_INVALID, "peer_alloc: NULL argument or zero size");
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "peer_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer_alloc: IPC handle");
+  }
+  *ptr = p;
+  return PA_OK;
+}
+
+int paged_attn_peer_free(void* ptr) {
+  g_err[0] = 0;
+  if (!ptr) return PA_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "peer_free");
+}
+
+int paged_attn_peer_open(const void* ipc_handle, void** ptr) {
+  g_err[0] = 0;
+  if (!ptr || !ipc_handle) return fail(PA_ERR_INVALID, "peer_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "peer_open: cudaIpcOpenMemHandle");
+}
+
+int paged_attn_peer_close(void* ptr) {
+  g_err[0] = 0;
+  if (!ptr) return PA_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "peer_close");
+}
+
+int paged_attn_decode_peers(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
+                            size_t workspace_bytes, void* const* o_peers, int32_t n_peers, int32_t* status,
+                            void* stream) {
+  g_err[0] = 0;
+  if (!o_peers || n_peers < 1 || n_peers > pa::kMaxPeers)
+    return fail(PA_ERR_INVALID, "decode_peers: 1..%d output pointers required", pa::kMaxPeers);
+  pa::AttnParams p;
+  int rc = build_attn(io, kv, pg, status, p);
+  if (rc) return rc;
+  for (int r = 0; r < n_peers; ++r) {
+    if (!o_peers[r] || !al(o_peers[r], 2)) return fail(PA_ERR_INVALID, "decode_peers: output %d NULL or misaligned", r);
+    p.o_peer[r] = o_peers[r];
+  }
+  p.n_peers = n_peers;
+  if (!use_decode(p))
+    return fail(PA_ERR_UNSUPPORTED, "decode_peers: max_q_len * (num_q_heads / num_kv_heads) must be <= %d", kNcMax);
+  return run_decode(p, kv, workspace, workspace_bytes, stream);
+}
+
+int paged_attn_peer_barrier(int32_t* local_flags, int32_t* const* peer_flags, int32_t n_peers, int32_t rank,
+                            int32_t epoch, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  if (!local_flags || !peer_flags || n_peers < 1 || n_peers > pa::kMaxPeers || rank < 0 || rank >= n_peers)
+    return fail(PA_ERR_INVALID, "peer_barrier: bad arguments");
+  pa::PeerFlags pf{};
+  for (int r = 0; r < n_peers; ++r) {
+    if (!peer_flags[r]) return fail(PA_ERR_INVALID, "peer_barrier: flag pointer %d is NULL", r);
+    pf.flag[r] = peer_flags[r];
+  }
+  cudaError_t e = pa::launch_peer_barrier(local_flags, pf, n_peers, rank, epoch, status,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "peer barrier launch");
+}
+
 int paged_attn_prefill(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
                        void* stream) {
   g_err[0] = 0;

@@ -840,14 +840,14 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
           if (complete) {
             const float inv = lt > 0.f ? 1.f / lt : 0.f;
             if (valid) {
-              __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, cp.b) + (cp.kvh * p.G + hq) * p.o_sh +
-                             static_cast<long long>(qi) * p.o_sm;
+              const long long orow = o_seq_base(p, cp.b) + (cp.kvh * p.G + hq) * p.o_sh +
+                                     static_cast<long long>(qi) * p.o_sm;
 #pragma unroll
               for (int mt = 0; mt < KS; ++mt)
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                   const int d = INT8 ? (D / 8) * r + 2 * mt + hf : 16 * mt + r + 8 * hf;
-                  orow[d] = __float2half_rn(acc[mt][nt][e + 2 * hf] * inv);
+                  store_o(p, orow + d, __float2half_rn(acc[mt][nt][e + 2 * hf] * inv));
                 }
               if (r == 0 && p.lse) {
                 const float L = lt > 0.f ? (m_run[nt][e] + lg2(lt)) * 0.6931471805599453f : -INFINITY;
@@ -877,6 +877,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
     cursor_next(p, s_ts, cp);
   }
   if constexpr (USE_CPASYNC) cp_async_wait<0>();
+  peer_store_fence(p);
 }
 
 // Combine the split-K partials of every segment that straddles warp ranges.
@@ -896,13 +897,13 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
     // no visible keys: O = 0, L = -inf
     for (int col = warp; col < ncols; col += 4) {
       const int qi = col / p.G, hq = col - (col / p.G) * p.G;
-      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh +
-                     static_cast<long long>(qi) * p.o_sm;
-      for (int d = lane; d < D; d += 32) orow[d] = __float2half_rn(0.f);
+      const long long orow = o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh + static_cast<long long>(qi) * p.o_sm;
+      for (int d = lane; d < D; d += 32) store_o(p, orow + d, __float2half_rn(0.f));
       if (lane == 0 && p.lse)
         static_cast<__half*>(p.lse)[l_seq_base(p, b) + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
             __float2half_rn(-INFINITY);
     }
+    peer_store_fence(p);
     return;
   }
   const int total = p.tstart[p.B] * p.Hkv;
@@ -935,16 +936,16 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
       for (int k = 0; k < D / 32; ++k) o[k] += po[lane + 32 * k] * f;
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
-    __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh +
-                   static_cast<long long>(qi) * p.o_sm;
+    const long long orow = o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh + static_cast<long long>(qi) * p.o_sm;
 #pragma unroll
-    for (int k = 0; k < D / 32; ++k) orow[lane + 32 * k] = __float2half_rn(o[k] * inv);
+    for (int k = 0; k < D / 32; ++k) store_o(p, orow + lane + 32 * k, __float2half_rn(o[k] * inv));
     if (lane == 0 && p.lse) {
       const float L = l > 0.f ? (M + lg2(l)) * 0.6931471805599453f : -INFINITY;
       static_cast<__half*>(p.lse)[l_seq_base(p, b) + (kvh * p.G + hq) * p.l_sh + static_cast<long long>(qi) * p.l_sm] =
           __float2half_rn(L);
     }
   }
+  peer_store_fence(p);
 }
 
 template <int D, int KVT, int QT, int NT, bool TMA>
@@ -1033,6 +1034,45 @@ int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, Deco
   if (D == 64) return plan_kv<64>(kv_kind, q_bf16, nt, B, use_tma != 0, out);
   if (D == 128) return plan_kv<128>(kv_kind, q_bf16, nt, B, use_tma != 0, out);
   return -1;
+}
+
+namespace {
+// One CTA: thread t posts `epoch` into slot `rank` of peer t's flags, then
+// waits for slot t of this GPU's flags to hold `epoch` (system-scope
+// release / acquire; each wait gives up after ~0.4 s with a status bit).
+__global__ void __launch_bounds__(32) pa_peer_barrier_kernel(int* local_flags, const PeerFlags peers, int n,
+                                                              int rank, int epoch, int* status) {
+  pdl_enter();
+  const int t = threadIdx.x;
+  if (t < n) {
+    asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+    asm volatile("st.release.sys.global.b32 [%0], %1;\n" ::"l"(peers.flag[t] + rank), "r"(epoch) : "memory");
+  }
+  __syncwarp();
+  if (t < n) {
+    bool ok = false;
+    for (int i = 0; i < (1 << 22); ++i) {
+      int v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];\n" : "=r"(v) : "l"(local_flags + t) : "memory");
+      if (v == epoch) {
+        ok = true;
+        break;
+      }
+      __nanosleep(100);
+    }
+    if (!ok) set_status(status, ST_PEER_TIMEOUT);
+  }
+  __syncwarp();
+}
+}  // namespace
+
+cudaError_t launch_peer_barrier(int* local_flags, const PeerFlags& peers, int n, int rank, int epoch, int* status,
+                                cudaStream_t stream) {
+  if (n < 1 || n > kMaxPeers) return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl(pa_peer_barrier_kernel, dim3(1), dim3(32), 0, stream, local_flags, peers, n, rank, epoch,
+                             status);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,

@@ -127,6 +127,21 @@ __device__ __forceinline__ long long o_seq_base(const AttnParams& p, int b) {
 __device__ __forceinline__ long long l_seq_base(const AttnParams& p, int b) {
   return p.q_start ? static_cast<long long>(p.q_start[b]) * p.l_sm : static_cast<long long>(b) * p.l_sb;
 }
+// Store one O element at element offset `idx` from p.o: locally, or into
+// every GPU of a peer output exchange (NVLink stores to mapped peer memory).
+__device__ __forceinline__ void store_o(const AttnParams& p, long long idx, __half v) {
+  if (p.n_peers == 0) {
+    static_cast<__half*>(p.o)[idx] = v;
+    return;
+  }
+#pragma unroll 1
+  for (int r = 0; r < p.n_peers; ++r) static_cast<__half*>(p.o_peer[r])[idx] = v;
+}
+// End of a kernel that stored O to peers: its stores are performed system-wide
+// before the barrier kernel that follows posts its flags.
+__device__ __forceinline__ void peer_store_fence(const AttnParams& p) {
+  if (p.n_peers) __threadfence_system();
+}
 // Query rows of sequence b: q_len clamped to max_q_len and, for ragged rows,
 // to the rows left in Q after q_start[b] (0 for a start outside [0, T)), so
 // bad metadata can never address past Q, O or L.

@@ -21,7 +21,9 @@ enum : int {
   ST_BAD_NUM_BLOCKS = 4,   // num_blocks_per_seq larger than the block table width
   ST_BAD_SEQ_INDEX = 8,    // token -> sequence index outside [0, num_seqs)
   ST_WAIT_TIMEOUT = 16,    // a bounded wait on an asynchronous copy gave up
+  ST_PEER_TIMEOUT = 32,    // the cross-GPU barrier gave up waiting for a peer's flag
 };
+constexpr int kMaxPeers = 8;  // GPUs of one box taking part in a peer output exchange
 
 // TMA descriptors of the K and V pools (4-D maps over [block, slot, head, d]).
 struct alignas(64) KvMaps {
@@ -57,7 +59,11 @@ struct AttnParams {
   const int* nblk;
   const int* qlen;
   const int* kvlen;
-  // Outputs: O [B, Hq, maxq, D] fp16, L [B, Hq, maxq] fp16
+  // Outputs: O [B, Hq, maxq, D] fp16, L [B, Hq, maxq] fp16.  With n_peers > 0
+  // every O element goes to o_peer[0..n_peers) at its offset from o instead
+  // (the same position in each GPU's output buffer, mapped into this process).
+  void* o_peer[kMaxPeers];
+  int n_peers;
   void* o;
   long long o_sb, o_sh, o_sm;
   void* lse;
@@ -116,6 +122,14 @@ int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, Deco
 // DECODE_SPLIT only the split kernel, DECODE_MERGE only the merge kernel (over
 // the workspace a DECODE_SPLIT launch with the same problem filled).
 enum : int { DECODE_BOTH = 0, DECODE_SPLIT = 1, DECODE_MERGE = 2 };
+// Cross-GPU barrier of a peer output exchange: post `epoch` into slot `rank`
+// of every peer's flag array, then wait (bounded) until every slot of this
+// GPU's array holds `epoch`.
+struct PeerFlags {
+  int* flag[kMaxPeers];
+};
+cudaError_t launch_peer_barrier(int* local_flags, const PeerFlags& peers, int n, int rank, int epoch, int* status,
+                                cudaStream_t stream);
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
                           const DecodeLaunch& plan, cudaStream_t stream, int phase = DECODE_BOTH);
 cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);

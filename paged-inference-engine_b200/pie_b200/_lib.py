@@ -28,6 +28,7 @@ PA_STATUS_BAD_BLOCK_ID = 1
 PA_STATUS_BAD_POSITION = 2
 PA_STATUS_BAD_NUM_BLOCKS = 4
 PA_STATUS_BAD_SEQ_INDEX = 8
+PA_STATUS_PEER_TIMEOUT = 32
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -96,6 +97,15 @@ SIGNATURES = {
     "paged_attn_varlen": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
                                          ctypes.POINTER(PaPaging), _vp, ctypes.c_int32, _vp, ctypes.c_size_t,
                                          _vp, _vp]),
+    "paged_attn_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _vp]),
+    "paged_attn_peer_free": (ctypes.c_int, [_vp]),
+    "paged_attn_peer_open": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p)]),
+    "paged_attn_peer_close": (ctypes.c_int, [_vp]),
+    "paged_attn_decode_peers": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
+                                               ctypes.POINTER(PaPaging), _vp, ctypes.c_size_t,
+                                               ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, _vp, _vp]),
+    "paged_attn_peer_barrier": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32, ctypes.c_int32,
+                                               ctypes.c_int32, _vp, _vp]),
     "paged_attn_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
                                                  ctypes.POINTER(PaPaging), _vp, _vp]),
     "paged_attn_prefill": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),

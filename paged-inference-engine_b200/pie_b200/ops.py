@@ -145,6 +145,8 @@ def _raise_status(fn: str, st: torch.Tensor) -> None:
             bits.append("num_blocks_per_seq wider than the block table")
         if v & _lib.PA_STATUS_BAD_SEQ_INDEX:
             bits.append("sequence index outside the block table")
+        if v & _lib.PA_STATUS_PEER_TIMEOUT:
+            bits.append("a peer GPU never reached the output-exchange barrier")
         st.zero_()
         raise IndexError(f"{fn}: device status {v:#x}: " + "; ".join(bits))
 
@@ -290,6 +292,53 @@ def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch
     if _CHECK and status is not None:
         _raise_status("paged_attention_varlen", status)
     return out, lse
+
+
+def paged_attention_peers(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per_seq: torch.Tensor,
+                          block_table: torch.Tensor, num_blocks_per_seq: torch.Tensor, block_size: int,
+                          kv_len_per_seq: torch.Tensor, k_scale: Optional[torch.Tensor], v_scale: Optional[torch.Tensor],
+                          out: torch.Tensor, out_peer_ptrs: list[int], *,
+                          status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode whose O rows go to every GPU of a peer exchange (paged_attn_decode_peers).
+
+    ``out`` is this GPU's view of the destination (it fixes the layout);
+    ``out_peer_ptrs[r]`` is the address of the same element 0 in GPU r's
+    mapped buffer.  Returns the local LSE [B, Hq, q] (fp16).
+    """
+    B, Hq, maxq, D = Q.shape
+    dev = Q.device
+    if Q.stride(3) != 1:
+        Q = Q.contiguous()
+    keep: list = []
+    kc = kv_cache_desc(K, V, k_scale, v_scale)
+    pg = paging_desc(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq, keep)
+    if out.dtype != torch.float16 or tuple(out.shape) != (B, Hq, maxq, D):
+        raise ValueError("out must be float16 with Q's shape")
+    lse = torch.empty((B, Hq, maxq), dtype=torch.float16, device=dev)
+    io = PaAttnIO()
+    io.q = Q.data_ptr()
+    io.q_dtype = _TORCH2PA[Q.dtype]
+    io.num_q_heads, io.max_q_len = Hq, maxq
+    io.q_stride_seq, io.q_stride_head, io.q_stride_row = Q.stride(0), Q.stride(1), Q.stride(2)
+    io.o = out.data_ptr()
+    io.o_stride_seq, io.o_stride_head, io.o_stride_row = out.stride(0), out.stride(1), out.stride(2)
+    io.lse = lse.data_ptr()
+    io.l_stride_seq, io.l_stride_head, io.l_stride_row = lse.stride(0), lse.stride(1), lse.stride(2)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if status is None and _CHECK:
+        status = status_word(dev)
+    peers = (ctypes.c_void_p * len(out_peer_ptrs))(*out_peer_ptrs)
+    with torch.cuda.device(dev):
+        nbytes = ctypes.c_size_t(0)
+        _lib.check("paged_attn_workspace_size", lib.paged_attn_workspace_size(io, kc, pg, ctypes.byref(nbytes)))
+        ws = workspace(dev, nbytes.value) if nbytes.value else None
+        _lib.check("paged_attn_decode_peers",
+                   lib.paged_attn_decode_peers(io, kc, pg, _ptr(ws), 0 if ws is None else ws.numel(), peers,
+                                               len(out_peer_ptrs), _ptr(status), stream))
+    if _CHECK and status is not None:
+        _raise_status("paged_attention_peers", status)
+    return lse
 
 
 def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor, seq_index: torch.Tensor,

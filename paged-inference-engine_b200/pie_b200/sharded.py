@@ -12,6 +12,8 @@ the paged-attention hot path (kernels/flash_attention.py:139-172 per rank).
 """
 from __future__ import annotations
 
+import ctypes
+import math
 from typing import Callable, Optional
 
 import torch
@@ -25,6 +27,80 @@ def head_range(num_heads: int, world: int, rank: int) -> tuple[int, int]:
     return rank * n, (rank + 1) * n
 
 
+class _DeviceBuffer:
+    """A raw device allocation presented to torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerOutputExchange:
+    """Output buffers of every rank mapped into every rank (plain CUDA IPC peer mappings).
+
+    Two fp16 output buffers (steps alternate between them, so a rank never
+    overwrites rows a peer may still be reading) and one int32 flag array per
+    rank.  Set-up is collective: every rank calls ``ensure`` with the same shape.
+    """
+
+    def __init__(self, group, world: int, rank: int, device: torch.device):
+        self.group, self.world, self.rank, self.device = group, world, rank, device
+        self.shape = None
+        self.epoch = 0
+
+    def ensure(self, shape: tuple[int, ...]) -> None:
+        if self.shape == tuple(shape):
+            return
+        if self.shape is not None:
+            raise RuntimeError("the peer output buffers were set up for another shape")
+        from . import _lib
+
+        lib = _lib.load()
+        nbytes = math.prod(shape) * 2
+        local, handles = [], []
+        with torch.cuda.device(self.device):
+            for size in (nbytes, nbytes, 256):
+                ptr, h = ctypes.c_void_p(), (ctypes.c_char * 64)()
+                _lib.check("paged_attn_peer_alloc", lib.paged_attn_peer_alloc(size, ctypes.byref(ptr), h))
+                local.append(ptr.value)
+                handles.append(bytes(h))
+            all_h: list = [None] * self.world
+            dist.all_gather_object(all_h, handles, group=self.group)
+            peers = [[0] * self.world for _ in range(3)]
+            for r in range(self.world):
+                for k in range(3):
+                    if r == self.rank:
+                        peers[k][r] = local[k]
+                        continue
+                    ptr = ctypes.c_void_p()
+                    _lib.check("paged_attn_peer_open", lib.paged_attn_peer_open(all_h[r][k], ctypes.byref(ptr)))
+                    peers[k][r] = ptr.value
+        self.local, self.peers = local, peers
+        self.views = [torch.as_tensor(_DeviceBuffer(local[k], shape, "<f2"), device=self.device) for k in range(2)]
+        self.flags = (ctypes.c_void_p * self.world)(*peers[2])
+        self.shape = tuple(shape)
+        dist.barrier(group=self.group)  # every rank has mapped every buffer before the first exchange
+
+    def exchange(self, run_decode: Callable[[torch.Tensor, list[int]], None], head_lo: int, head_hi: int,
+                 status: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """run_decode(out_view, peer_ptrs) writes heads [head_lo, head_hi) into every rank; returns all heads."""
+        from . import _lib
+
+        lib = _lib.load()
+        k = self.epoch & 1
+        self.epoch += 1
+        full = self.views[k]
+        view = full[:, head_lo:head_hi]
+        off = view.data_ptr() - full.data_ptr()
+        run_decode(view, [p + off for p in self.peers[k]])
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        st = None if status is None else status.data_ptr()
+        _lib.check("paged_attn_peer_barrier",
+                   lib.paged_attn_peer_barrier(self.local[2], self.flags, self.world, self.rank, self.epoch, st,
+                                               stream))
+        return full
+
+
 class KVHeadShardedDecoder:
     """Per-rank decode over the local KV heads + all-gather of head outputs.
 
@@ -32,10 +108,21 @@ class KVHeadShardedDecoder:
     kv_len, k_scale, v_scale) -> (O, L)`` computes the local heads; it defaults
     to the CUDA ``flash_attention_forward``.  The gather uses the default
     process group (NCCL on GPUs; any backend works for the host logic).
+
+    ``exchange="peer"`` (GPUs of one box, decode shapes) replaces the
+    all-gather by the fused exchange: the decode kernels store every finished
+    output row into every rank's mapped output buffer and a cross-GPU flag
+    barrier ends the step.  The returned tensor is then one of two buffers the
+    steps alternate between: consume it on the current stream before the
+    next-but-one ``forward``.
     """
 
     def __init__(self, num_q_heads: int, num_kv_heads: int, head_dim: int, group=None,
-                 attention_fn: Optional[Callable] = None):
+                 attention_fn: Optional[Callable] = None, exchange: str = "nccl"):
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
+        self.exchange = exchange
+        self._peer: Optional[PeerOutputExchange] = None
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -57,11 +144,28 @@ class KVHeadShardedDecoder:
     def forward(self, Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale=None,
                 v_scale=None, gather: bool = True):
         """Returns O for all heads [B, Hq, q, D] (gather=True) or the local heads."""
+        if gather and self.world > 1 and self.exchange == "peer":
+            return self._forward_peer(Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale,
+                                      v_scale)
         O_loc, _ = self.attention_fn(Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale,
                                      v_scale)
         if not gather or self.world == 1:
             return O_loc
         return self.gather(O_loc)
+
+    def _forward_peer(self, Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale, v_scale):
+        from . import ops
+
+        B, hl, q, D = Q_local.shape
+        if self._peer is None:
+            self._peer = PeerOutputExchange(self.group, self.world, self.rank, Q_local.device)
+        self._peer.ensure((B, self.Hq, q, D))
+
+        def run(view, ptrs):
+            ops.paged_attention_peers(Q_local, K, V, q_len, block_table, num_blocks, int(block_size), kv_len,
+                                      k_scale, v_scale, view, ptrs)
+
+        return self._peer.exchange(run, self.q_lo, self.q_hi)
 
     def gather(self, O_loc: torch.Tensor) -> torch.Tensor:
         B, hl, q, D = O_loc.shape

@@ -1,0 +1,64 @@
+"""Fused head-output exchange (stores into peer buffers) against the NCCL all-gather.
+
+Two ranks on two GPUs of one box, each holding half of the KV heads of a
+long-context INT8 pool.  Three decode steps with different queries (the peer
+path alternates between its two output buffers) must give, on every rank, the
+same bytes as the NCCL all-gather path.  Skipped where fewer than two GPUs are
+visible (the single-GPU runs of this suite).
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank(rank, world, port):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "paged-inference-engine_b200"))
+    import torch.distributed as dist
+    from pie_b200.sharded import KVHeadShardedDecoder, build_rank_pool
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        Bn, Hq, Hkv, D, BS = 16, 16, 4, 128, 16
+        ctx = [300 + 97 * i for i in range(Bn)]
+        K, V, ks, vs, bt, nblk, NB = build_rank_pool(ctx, Hkv // world, D, BS, 500 + rank, dev)
+        ql = torch.ones(Bn, dtype=torch.int32, device=dev)
+        kl = torch.tensor(ctx, dtype=torch.int32, device=dev)
+        ref = KVHeadShardedDecoder(Hq, Hkv, D)
+        peer = KVHeadShardedDecoder(Hq, Hkv, D, exchange="peer")
+        for step in range(3):
+            Qf = torch.randn(Bn, Hq, 1, D, generator=torch.Generator().manual_seed(70 + step)).half().to(dev)
+            Ql = ref.local_q(Qf).contiguous()
+            want = ref.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs).clone()
+            got = peer.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs).clone()
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), f"rank {rank} step {step}: max diff {(got.float() - want.float()).abs().max()}"
+        dist.barrier()
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one box")
+def test_peer_exchange_matches_all_gather():
+    mp.spawn(_rank, args=(2, _free_port()), nprocs=2, join=True)
