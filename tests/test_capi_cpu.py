@@ -152,3 +152,60 @@ def test_scale_layouts_become_strides():
     M = torch.zeros(5, 4, 16, 64, dtype=torch.float16)
     d = ops.kv_cache_desc(M, M)
     assert (d.k_stride_block, d.k_stride_slot, d.k_stride_head) == (4096, 1024, 64)
+
+
+def test_varlen_and_peer_entry_points_validate_without_gpu():
+    """The ragged-row and peer-exchange entry points reject bad arguments before any CUDA call."""
+    import ctypes
+
+    from pie_b200 import _lib
+
+    lib = _lib.load()
+    io, kv, pg = _descs()
+    # ragged rows: q_start is required, the row count must not be negative, T = 0 is a no-op
+    assert lib.paged_attn_varlen(io, kv, pg, None, 10, None, 0, None, None) == _lib.PA_ERR_INVALID
+    assert b"q_start" in lib.paged_attn_error_string()
+    assert lib.paged_attn_varlen(io, kv, pg, 1 << 23, -1, None, 0, None, None) == _lib.PA_ERR_INVALID
+    assert lib.paged_attn_varlen(io, kv, pg, 1 << 23, 0, None, 0, None, None) == _lib.PA_OK
+    # peer decode: 1..8 output pointers, decode shapes only
+    none = (ctypes.c_void_p * 1)()
+    assert lib.paged_attn_decode_peers(io, kv, pg, None, 0, none, 0, None, None) == _lib.PA_ERR_INVALID
+    nine = (ctypes.c_void_p * 9)(*([1 << 24] * 9))
+    assert lib.paged_attn_decode_peers(io, kv, pg, None, 0, nine, 9, None, None) == _lib.PA_ERR_INVALID
+    two = (ctypes.c_void_p * 2)(1 << 24, 1 << 25)
+    assert lib.paged_attn_decode_peers(io, kv, pg, None, 0, two, 2, None, None) == _lib.PA_ERR_UNSUPPORTED
+    assert b"max_q_len" in lib.paged_attn_error_string()  # max_q_len 64 x group 4 is a prefill shape
+    # barrier: rank inside [0, n), every flag pointer present
+    flags = (ctypes.c_void_p * 2)(1 << 24, None)
+    assert lib.paged_attn_peer_barrier(1 << 24, flags, 2, 2, 1, None, None) == _lib.PA_ERR_INVALID
+    assert lib.paged_attn_peer_barrier(1 << 24, flags, 2, 0, 1, None, None) == _lib.PA_ERR_INVALID
+    assert b"flag pointer 1" in lib.paged_attn_error_string()
+    # set-up helpers reject NULL outputs
+    assert lib.paged_attn_peer_alloc(64, None, None) == _lib.PA_ERR_INVALID
+    assert lib.paged_attn_peer_open(None, None) == _lib.PA_ERR_INVALID
+    assert lib.paged_attn_peer_free(None) == _lib.PA_OK and lib.paged_attn_peer_close(None) == _lib.PA_OK
+
+
+def test_varlen_front_end_checks_shapes():
+    from pie_b200 import ops
+
+    K = torch.zeros(2, 16, 2, 64, dtype=torch.float16)
+    i = torch.ones(2, dtype=torch.int32)
+    bt = torch.zeros(2, 1, dtype=torch.int32)
+    with pytest.raises(ValueError, match="total_q_rows"):
+        ops.paged_attention_varlen(torch.zeros(1, 4, 2, 64), torch.zeros(3, dtype=torch.int32), K, K, bt, i, 16, i)
+    with pytest.raises(ValueError, match="3 offsets"):
+        ops.paged_attention_varlen(torch.zeros(4, 2, 64), torch.zeros(2, dtype=torch.int32), K, K, bt, i, 16, i)
+    with pytest.raises(ValueError, match="block_size"):
+        ops.paged_attention_varlen(torch.zeros(4, 2, 64), torch.zeros(3, dtype=torch.int32), K, K, bt, i, 8, i)
+
+
+def test_sharded_decoder_exchange_option():
+    from pie_b200.sharded import KVHeadShardedDecoder
+
+    with pytest.raises(ValueError, match="exchange"):
+        KVHeadShardedDecoder(8, 2, 64, attention_fn=lambda *a: None, exchange="ring")
+    dec = KVHeadShardedDecoder(8, 2, 64, attention_fn=lambda *a: (torch.ones(1, 8, 1, 64), None), exchange="peer")
+    # a single process takes the local path: no exchange, no GPU
+    out = dec.forward(torch.zeros(1, 8, 1, 64), None, None, None, None, None, 16, None)
+    assert out.shape == (1, 8, 1, 64)
