@@ -81,6 +81,25 @@ class PeerOutputExchange:
         self.shape = tuple(shape)
         dist.barrier(group=self.group)  # every rank has mapped every buffer before the first exchange
 
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: no exchange may be in flight)."""
+        if self.shape is None:
+            return
+        from . import _lib
+
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no peer still writes into this rank's buffers
+        with torch.cuda.device(self.device):
+            for k in range(3):
+                for r in range(self.world):
+                    if r != self.rank:
+                        _lib.check("paged_attn_peer_close", lib.paged_attn_peer_close(self.peers[k][r]))
+            dist.barrier(group=self.group)  # every peer has unmapped before the memory is freed
+            for k in range(3):
+                _lib.check("paged_attn_peer_free", lib.paged_attn_peer_free(self.local[k]))
+        self.shape, self.views = None, None
+
     def exchange(self, run_decode: Callable[[torch.Tensor, list[int]], None], head_lo: int, head_hi: int,
                  status: Optional[torch.Tensor] = None) -> torch.Tensor:
         """run_decode(out_view, peer_ptrs) writes heads [head_lo, head_hi) into every rank; returns all heads."""
@@ -136,6 +155,12 @@ class KVHeadShardedDecoder:
             attention_fn = flash_attention_forward
         self.attention_fn = attention_fn
         self._gather_buf = None
+
+    def close(self) -> None:
+        """Release the peer-exchange buffers (collective; a no-op for the NCCL exchange)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def local_q(self, Q_full: torch.Tensor) -> torch.Tensor:
         """This rank's query heads of a full [B, Hq, q, D] tensor."""

@@ -53,6 +53,7 @@ def _rank(rank, world, port):
             got = peer.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs).clone()
             torch.cuda.synchronize()
             assert torch.equal(got, want), f"rank {rank} step {step}: max diff {(got.float() - want.float()).abs().max()}"
+        peer.close()
         dist.barrier()
     finally:
         torch.cuda.synchronize()
