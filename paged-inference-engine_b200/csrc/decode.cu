@@ -914,27 +914,38 @@ __global__ void __launch_bounds__(128) pa_decode_merge_kernel(const AttnParams p
   const int w0 = S0 / chunk;
   const int w1 = (S1 - 1) / chunk;
   if (w0 == w1) return;  // written directly by the split kernel
+  // slot of warp w's partial for this segment: its second slot when the segment starts inside w's range
+  auto slot_of = [&](int w) { return (w == w0 && w0 * chunk < S0) ? 2 * w + 1 : 2 * w; };
   for (int col = warp; col < ncols; col += 4) {
     const int qi = col / p.G, hq = col - (col / p.G) * p.G;
+    // lane i reads partial w0 + i (32 at a time): the maxima and the sums are
+    // warp reductions instead of a chain of dependent L2 reads
     float M = -INFINITY;
-    for (int w = w0; w <= w1; ++w) {
-      const int slot = (w == w0 && w0 * chunk < S0) ? 2 * w + 1 : 2 * w;
-      M = fmaxf(M, p.part_ml[(static_cast<long long>(slot) * NC_MAX + col) * 2]);
-    }
+    for (int w = w0 + lane; w <= w1; w += 32)
+      M = fmaxf(M, p.part_ml[(static_cast<long long>(slot_of(w)) * NC_MAX + col) * 2]);
+    M = warp_max_xor(M, 1);
     const float Mu = (M == -INFINITY) ? 0.f : M;
     float l = 0.f;
     float o[D / 32];
 #pragma unroll
     for (int k = 0; k < D / 32; ++k) o[k] = 0.f;
-    for (int w = w0; w <= w1; ++w) {
-      const int slot = (w == w0 && w0 * chunk < S0) ? 2 * w + 1 : 2 * w;
-      const float* pm = p.part_ml + (static_cast<long long>(slot) * NC_MAX + col) * 2;
-      const float f = ex2(pm[0] - Mu);
-      l += pm[1] * f;
-      const float* po = p.part_o + (static_cast<long long>(slot) * NC_MAX + col) * D;
+    for (int base = w0; base <= w1; base += 32) {
+      float f = 0.f;
+      if (base + lane <= w1) {
+        const float* pm = p.part_ml + (static_cast<long long>(slot_of(base + lane)) * NC_MAX + col) * 2;
+        f = ex2(pm[0] - Mu);
+        l += pm[1] * f;
+      }
+      const int n = min(32, w1 - base + 1);
+#pragma unroll 4
+      for (int j = 0; j < n; ++j) {
+        const float fj = __shfl_sync(0xffffffffu, f, j);
+        const float* po = p.part_o + (static_cast<long long>(slot_of(base + j)) * NC_MAX + col) * D;
 #pragma unroll
-      for (int k = 0; k < D / 32; ++k) o[k] += po[lane + 32 * k] * f;
+        for (int k = 0; k < D / 32; ++k) o[k] += po[lane + 32 * k] * fj;
+      }
     }
+    l = warp_sum_xor(l, 1);
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const long long orow = o_seq_base(p, b) + (kvh * p.G + hq) * p.o_sh + static_cast<long long>(qi) * p.o_sm;
 #pragma unroll
