@@ -1,32 +1,41 @@
 """Benchmark of the B200 paged-attention hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_fp16|decode_int8|prefill_bf16|long_ctx_int8]
+                    [--workload long_ctx_int8|decode_fp16|decode_int8|prefill_bf16]
+                    [--exchange nccl|peer] [--no-extra] [--no-cpu-baseline]
 
 One step = one pass of the hot path over one batch of seeded synthetic input
 with the reference's benchmark shapes (no public dataset is involved):
 
-  decode_fp16   (default) paged decode attention, B=64, 32/8 heads, D=128,
-                block_size 16, ctx ~ U[512, 4096], fp16 KV.  Metric: HBM GB/s of
-                the algorithmic bytes (K/V of every attended token + Q + O).
+  long_ctx_int8 (default, every N) B=256, 64/8 heads, D=128, block_size 16,
+                ctx ~ U[8192, 32768], INT8 KV with fp16 per-token scales; the
+                KV heads are sharded across the N ranks (strong scaling) and
+                the per-head outputs gathered with an NCCL
+                all_gather_into_tensor inside the timed step.  Metric: HBM
+                GB/s of the algorithmic bytes (int8 K/V + scales of every
+                attended token, Q, O), whole job.
+  decode_fp16   paged decode attention, B=64, 32/8 heads, D=128, ctx ~
+                U[512, 4096], fp16 KV.  Metric: HBM GB/s.
   decode_int8   the same shape with INT8 KV (fp16 per-token scales, 1% outliers
                 x8): quantise-on-write of 64 new tokens per sequence, then decode.
   prefill_bf16  causal paged prefill, B=8, L ~ U[1024, 4096], 32/8 heads, bf16;
                 K/V written into scattered fp16 blocks, then attention.
                 Metric: TFLOP/s (causal FLOPs).
-  long_ctx_int8 B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8 KV; KV heads are
-                sharded across the N ranks and the per-head outputs gathered
-                with an NCCL all-gather (strong scaling).
 
-Decode workloads under torchrun run one batch per rank (seed + rank, weak
-scaling, no collective).  ``roofline`` describes the dominant launches: the
-attention call alone (no write kernel, no collective) on the same inputs,
-timed by a second CUDA-event loop after the timed region; its ``step_*``
-fields give the whole step against the same peak.  Inputs exceed the 126 MB L2 for every workload; the
-timed region is bracketed by barrier + synchronize, timed with CUDA events on
-the launching stream, max over ranks.  ``--impl reference`` times the
-reference's own path on the host CPU (the naive PyTorch paged attention,
-restated in oracle/) on the same workload and prints the same JSON line.
+On one GPU the line also carries, under ``workloads``, a full record (value,
+roofline, e2e, clocks, cpu_baseline) for each of the other three workloads,
+timed the same way in the same run.  ``roofline`` describes the dominant
+launches: the attention call alone (no write kernel, no collective) on the
+same inputs, timed by a second CUDA-event loop after the timed region; its
+``step_*`` fields give the whole step per GPU against the same peak.  Inputs
+exceed the 126 MB L2 for every workload; the timed region is bracketed by
+barrier + synchronize, timed with CUDA events on the launching stream, max
+over ranks.  ``e2e`` runs the same step through the public Python API with
+each step's inputs copied from pinned host memory and the result read back
+(for the sharded workload: every rank copies in its own query heads and
+metadata, rank 0 reads back the gathered output).  ``--impl reference`` times
+the reference's own path on the host CPU (the naive PyTorch paged attention,
+restated in oracle/) on the same workloads and prints the same JSON line.
 """
 from __future__ import annotations
 
@@ -152,6 +161,10 @@ class Workload:
     launches = 1
     h2d = d2h = 0
 
+    def io_bytes(self, ws: int) -> tuple[int, int]:
+        """(host->device, device->host) bytes of one e2e step, summed over the ranks."""
+        return self.h2d * ws, self.d2h * ws
+
     def cpu_sample(self, seconds: float, threads: int):
         torch.set_num_threads(threads)
         done, t, i = 0.0, 0.0, 0
@@ -179,7 +192,8 @@ class PipelinedInputs:
     the last read-back.
     """
 
-    def __init__(self, host: list, out_host: list, device):
+    def __init__(self, host: list, out_host: list, device, readback: bool = True):
+        self.readback = readback
         self.offs, total = [], 0
         for t in host:
             total = (total + 255) // 256 * 256
@@ -218,16 +232,17 @@ class PipelinedInputs:
             self.dbufs[s].copy_(self.hbuf, non_blocking=True)
             self.ready[s].record(self.h2d)
         cur.wait_event(self.ready[s])
-        if self.i >= 2:
+        if self.i >= 2 and self.readback:
             cur.wait_event(self.read[s])
         out = fn(s, self.views[s])
         self.free[s].record(cur)
         self.computed[s].record(cur)
-        out.record_stream(self.d2h)  # a per-call output stays allocated until it is read back
-        with torch.cuda.stream(self.d2h):
-            self.d2h.wait_event(self.computed[s])
-            self.out_host[s].copy_(out, non_blocking=True)
-            self.read[s].record(self.d2h)
+        if self.readback:
+            out.record_stream(self.d2h)  # a per-call output stays allocated until it is read back
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.computed[s])
+                self.out_host[s].copy_(out, non_blocking=True)
+                self.read[s].record(self.d2h)
         self.i += 1
 
 
@@ -334,6 +349,7 @@ class PrefillWorkload(Workload):
     def __init__(self, seed: int, device, cpu_only: bool = False):
         from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
 
+        self.name = "prefill_bf16"
         cfg = CONFIGS["prefill_bf16"]
         gen = torch.Generator().manual_seed(seed)
         L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
@@ -433,11 +449,15 @@ class PrefillWorkload(Workload):
 class LongCtxWorkload(Workload):
     """long_ctx_int8: B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8; KV heads sharded over ranks."""
 
-    def __init__(self, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl"):
+    def __init__(self, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl",
+                 batch: int = 0):
         from pie_b200.workloads import CONFIGS, draw_context_lengths
 
+        self.name = "long_ctx_int8"
         self.exchange = exchange
-        cfg = CONFIGS["long_ctx_int8"]
+        cfg = dict(CONFIGS["long_ctx_int8"])
+        if batch:
+            cfg["B"] = batch
         self.cfg = cfg
         Bn, Hq, Hkv, D, BS = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
         gen = torch.Generator().manual_seed(0)
@@ -474,17 +494,26 @@ class LongCtxWorkload(Workload):
         self.dominant = lambda: dec.forward(Ql, K, V, ql, bt, nblk, BS, kl, ks, vs, gather=False)
         self.dominant_work = self.work / self.ws  # this rank's KV heads, Q and O
 
+        # every rank copies in its own query heads and paging metadata; the
+        # gathered O (all heads) is read back once, by rank 0
         hO = [torch.empty(Bn, Hq, 1, D, dtype=torch.float16).pin_memory() for _ in range(2)]
         pipe = PipelinedInputs([dec.local_q(Qfull).contiguous(), bt.cpu(), nblk.cpu(), ql.cpu(), kl.cpu()], hO,
-                               device)
+                               device, readback=self.rank == 0)
         self.h2d = pipe.nbytes
         self.d2h = hO[0].numel() * hO[0].element_size()
+        self.dec = dec
 
         def run(s, v):
             return dec.forward(v[0], K, V, v[3], v[1], v[2], BS, v[4], ks, vs)
 
         self.e2e_step = lambda: pipe.step(run)
         self.e2e_start, self.e2e_end = pipe.start, pipe.end
+
+    def io_bytes(self, ws: int) -> tuple[int, int]:
+        return self.h2d * ws, self.d2h
+
+    def close(self):
+        self.dec.close()
 
     def cpu_unit(self, i):
         """One sequence of the workload's shape (ctx from its range) over all 8 KV heads."""
@@ -507,11 +536,12 @@ class LongCtxWorkload(Workload):
         return f"{n} sequences (4 distinct, ctx from the workload's range, all 8 KV heads), {t:.1f} s"
 
 
-def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl") -> Workload:
+def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl",
+                  batch: int = 0) -> Workload:
     if name == "prefill_bf16":
         return PrefillWorkload(1000 + rank, device, cpu_only)
     if name == "long_ctx_int8":
-        return LongCtxWorkload(ws, rank, device, cpu_only, exchange)
+        return LongCtxWorkload(ws, rank, device, cpu_only, exchange, batch)
     return DecodeWorkload(name, 1000 + rank, device, cpu_only)
 
 
@@ -559,37 +589,15 @@ def read_traffic(name: str):
     return None
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode_fp16",
-                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "long_ctx_int8"])
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
-                    help="long_ctx_int8 head-output exchange: NCCL all-gather or stores into peer buffers")
-    a = ap.parse_args()
-    a.warmup = max(3, a.warmup)
-
-    ws, rank, local = dist_env()
-    if a.impl == "reference":
-        return run_reference(a, ws, rank)
-
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if ws > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    peaks, peak_kind = load_peaks()
-    w = make_workload(a.workload, ws, rank, device, exchange=a.exchange)
+def measure(w: Workload, a, device, ws: int, rank: int, local: int, peaks: dict, peak_kind: str,
+            cpu_baseline: bool) -> dict:
+    """Time one workload: the step (``value``), its dominant launches alone (``roofline``),
+    the public-API step with host buffers (``e2e``), clocks during the timed
+    region, and (rank 0, one GPU) the reference's CPU path on a bounded sample."""
     if w.bound == "hbm":
         peak, punit = peaks["hbm_gbs"], "GB/s"
     else:
         peak, punit = peaks["bf16_tflops"], "TFLOP/s"
-
     with ClockSampler(local) as clk:
         ms = time_steps(w.step, a.steps, a.warmup, device, ws)
     ms_step = ms / a.steps
@@ -605,22 +613,20 @@ def main():
     e2e_steps = max(10, a.steps // 10)
     e_ms = time_steps(w.e2e_step, e2e_steps, a.warmup, device, ws, getattr(w, "e2e_start", None),
                       getattr(w, "e2e_end", None)) / e2e_steps
-    e2e = {"value": round(total_work / (e_ms * 1e-3) * w.scale, 2), "unit": w.unit, "h2d_bytes_per_step": w.h2d,
-           "d2h_bytes_per_step": w.d2h, "steps": e2e_steps, "ms_per_step": round(e_ms, 5)}
-
-    line = {
-        "metric": w.metric, "value": round(value, 2), "unit": w.unit, "n_gpus": ws, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": round(ms_step, 5), "us_per_step": round(ms_step * 1e3, 2),
-        "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": w.dtype,
-        "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
-        "config": {"workload": a.workload, **w.info,
+    e2e = {"value": round(total_work / (e_ms * 1e-3) * w.scale, 2), "unit": w.unit,
+           "h2d_bytes_per_step": w.io_bytes(ws)[0], "d2h_bytes_per_step": w.io_bytes(ws)[1],
+           "steps": e2e_steps, "ms_per_step": round(e_ms, 5)}
+    rec = {
+        "metric": w.metric, "value": round(value, 2), "unit": w.unit, "ms_per_step": round(ms_step, 5),
+        "us_per_step": round(ms_step * 1e3, 2), "higher_is_better": True, "scaling": w.scaling, "dtype": w.dtype,
+        "config": {"workload": w.name, **w.info,
                    "parallelism": ((f"kv-head shard x{ws} + " +
-                                    ("NCCL all_gather" if getattr(w, "exchange", "nccl") == "nccl"
+                                    ("NCCL all_gather_into_tensor" if getattr(w, "exchange", "nccl") == "nccl"
                                      else "output rows stored into peer buffers")) if w.scaling == "strong"
                                    else f"dp{ws} (one batch per rank)"),
                    "l2": "inputs larger than L2 (126 MB)"},
         "roofline": {"bound": w.bound, "achieved": round(dom, 2), "peak": peak, "unit": punit,
-                     "frac": round(dom / peak, 4), "traffic": read_traffic(f"{a.workload}_dominant_kernel"),
+                     "frac": round(dom / peak, 4), "traffic": read_traffic(f"{w.name}_dominant_kernel"),
                      "kernel": w.dominant_name, "us_per_launch": round(dom_ms * 1e3, 2),
                      "step_achieved": round(per_gpu, 2), "step_frac": round(per_gpu / peak, 4),
                      "step_kernels": w.kernel, "peak_source": f"{peak_kind} MEASURED_PEAKS"},
@@ -628,11 +634,68 @@ def main():
         "gpu_launches": w.launches * a.steps,
         "clocks": clk.summary(),
     }
-    if rank == 0 and ws == 1 and not a.no_cpu_baseline:
+    if cpu_baseline and rank == 0 and ws == 1:
         threads = os.cpu_count() or 1
         t, done, n = w.cpu_sample(a.cpu_seconds, threads)
-        line["cpu_baseline"] = {"value": round(done / t * w.scale, 4), "unit": w.unit, "cores": threads,
-                                "kind": "port", "sample": w.sample_desc(n, t)}
+        rec["cpu_baseline"] = {"value": round(done / t * w.scale, 4), "unit": w.unit, "cores": threads,
+                               "kind": "port", "sample": w.sample_desc(n, t)}
+    return rec
+
+
+EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="long_ctx_int8",
+                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "long_ctx_int8"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="one GPU: skip the records of the other workloads under the 'workloads' key")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="long_ctx_int8 head-output exchange: NCCL all-gather or stores into peer buffers")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="long_ctx_int8 with fewer sequences (same context-length draws), for small profiler "
+                         "captures; 0 = the workload's 256")
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+
+    ws, rank, local = dist_env()
+    if a.impl == "reference":
+        return run_reference(a, ws, rank)
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    peaks, peak_kind = load_peaks()
+    w = make_workload(a.workload, ws, rank, device, exchange=a.exchange, batch=a.batch)
+    rec = measure(w, a, device, ws, rank, local, peaks, peak_kind, not a.no_cpu_baseline)
+    close = getattr(w, "close", None)
+    if close is not None:
+        close()
+    del w
+    torch.cuda.empty_cache()
+    line = {"metric": rec.pop("metric"), "value": rec.pop("value"), "unit": rec.pop("unit"), "n_gpus": ws,
+            "steps": a.steps, "warmup": a.warmup, **rec, "vs_baseline": None,
+            "data": "synthetic (seeded N(0,1), reference benchmark shapes)"}
+    if ws == 1 and not a.no_extra:
+        # the other configurations of the reference's measurement plan, timed the same way in this run
+        line["workloads"] = {}
+        for name in EXTRA_WORKLOADS:
+            if name == a.workload:
+                continue
+            wx = make_workload(name, ws, rank, device)
+            line["workloads"][name] = measure(wx, a, device, ws, rank, local, peaks, peak_kind,
+                                              not a.no_cpu_baseline)
+            del wx
+            torch.cuda.empty_cache()
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -651,24 +714,30 @@ def run_reference(a, ws, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    w = make_workload(a.workload, ws, rank, None, cpu_only=True)
-    budget = min(2.0, 120.0 / max(1, a.steps + a.warmup))
-    for _ in range(a.warmup):
-        w.cpu_sample(0.0, threads)
-    t_tot, done_tot, n_tot = 0.0, 0.0, 0
-    for _ in range(a.steps):
-        t, done, n = w.cpu_sample(budget, threads)
-        t_tot, done_tot, n_tot = t_tot + t, done_tot + done, n_tot + n
-    val = done_tot / t_tot * w.scale
-    sample = f"{a.steps} steps of {budget * 1e3:.0f} ms: " + w.sample_desc(n_tot, t_tot)
-    line = {"impl": "reference", "metric": w.metric, "value": round(val, 4), "unit": w.unit, "n_gpus": ws,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_tot / a.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
-            "config": {"workload": a.workload, **w.info, "threads": threads},
-            "cpu_baseline": {"value": round(val, 4), "unit": w.unit, "cores": threads, "kind": "port",
-                             "sample": sample},
-            "e2e": {"value": round(val, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+    def timed(name, budget):
+        w = make_workload(name, ws, rank, None, cpu_only=True)
+        for _ in range(a.warmup):
+            w.cpu_sample(0.0, threads)
+        t_tot, done_tot, n_tot = 0.0, 0.0, 0
+        for _ in range(a.steps):
+            t, done, n = w.cpu_sample(budget, threads)
+            t_tot, done_tot, n_tot = t_tot + t, done_tot + done, n_tot + n
+        val = done_tot / t_tot * w.scale
+        sample = f"{a.steps} steps of {budget * 1e3:.0f} ms: " + w.sample_desc(n_tot, t_tot)
+        return {"impl": "reference", "metric": w.metric, "value": round(val, 4), "unit": w.unit, "n_gpus": ws,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(t_tot / a.steps * 1e3, 3),
+                "higher_is_better": True, "scaling": w.scaling, "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded N(0,1), reference benchmark shapes)",
+                "config": {"workload": name, **w.info, "threads": threads},
+                "cpu_baseline": {"value": round(val, 4), "unit": w.unit, "cores": threads, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(val, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+    line = timed(a.workload, min(2.0, 120.0 / max(1, a.steps + a.warmup)))
+    if ws == 1 and not a.no_extra:
+        line["workloads"] = {n: timed(n, min(0.5, 30.0 / max(1, a.steps + a.warmup)))
+                             for n in EXTRA_WORKLOADS if n != a.workload}
     print(json.dumps(line))
 
 

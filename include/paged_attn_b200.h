@@ -70,7 +70,13 @@ enum {
  * Paged KV pool.  Replaces the cache buffers of transformer/model.py:62-67
  * and the K/V/scale arguments of kernels/flash_attention.py:21-33.
  *   k, v            logical [num_blocks, block_size, num_kv_heads, head_dim]
- *   dtype           PA_DTYPE_F16, PA_DTYPE_BF16 or PA_DTYPE_I8
+ *   dtype           PA_DTYPE_F16, PA_DTYPE_BF16, PA_DTYPE_I8 or PA_DTYPE_F32.
+ *                   fp32 pools (the reference kernel accepts any float pool,
+ *                   kernels/flash_attention.py:79-84) are read by the tiled
+ *                   kernel only, rounded to fp16 operands in shared memory
+ *                   (TF32's 11-bit significand, the precision of the
+ *                   reference's tl.dot); |values| must stay below 65520.
+ *                   The split-K decode entry points reject them.
  *   k_scale/v_scale dequantisation scales, required for PA_DTYPE_I8 and
  *                   ignored otherwise.  Per-(token, head) scales use all three
  *                   strides; the reference's per-(block, head) scales

@@ -58,8 +58,9 @@ constexpr int kMaxDecodeSeqs = 8192;
 // Validate a KV pool; fills the pool part of AttnParams / WriteParams.
 int check_cache(const pa_kv_cache_t* kv) {
   if (!kv) return fail(PA_ERR_INVALID, "kv cache descriptor is NULL");
-  if (kv->dtype != PA_DTYPE_F16 && kv->dtype != PA_DTYPE_BF16 && kv->dtype != PA_DTYPE_I8)
-    return fail(PA_ERR_INVALID, "KV pool dtype %d unsupported (fp16, bf16 or int8)", kv->dtype);
+  if (kv->dtype != PA_DTYPE_F16 && kv->dtype != PA_DTYPE_BF16 && kv->dtype != PA_DTYPE_I8 &&
+      kv->dtype != PA_DTYPE_F32)
+    return fail(PA_ERR_INVALID, "KV pool dtype %d unsupported (fp16, bf16, int8 or fp32)", kv->dtype);
   if (kv->head_dim != 64 && kv->head_dim != 128)
     return fail(PA_ERR_UNSUPPORTED, "head_dim %d not compiled (64 or 128)", kv->head_dim);
   if (!is_pow2(kv->block_size))
@@ -172,9 +173,16 @@ int build_attn(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_
   return PA_OK;
 }
 
-bool use_decode(const pa::AttnParams& p) { return p.maxq * p.G <= kNcMax && p.B <= kMaxDecodeSeqs; }
+// The split-K decode kernels read 16-bit and int8 pools; fp32 pools (a
+// reference-compatible format, not a serving one) always take the tiled kernel.
+bool use_decode(const pa::AttnParams& p, const pa_kv_cache_t* kv) {
+  return p.maxq * p.G <= kNcMax && p.B <= kMaxDecodeSeqs && kv->dtype != PA_DTYPE_F32;
+}
 int decode_nt(const pa::AttnParams& p) { return p.maxq * p.G <= 8 ? 1 : 2; }
-int kv_kind(int dtype) { return dtype == PA_DTYPE_F16 ? pa::KV_F16 : dtype == PA_DTYPE_BF16 ? pa::KV_BF16 : pa::KV_I8; }
+int kv_kind(int dtype) {
+  return dtype == PA_DTYPE_F16 ? pa::KV_F16 : dtype == PA_DTYPE_BF16 ? pa::KV_BF16
+                                            : dtype == PA_DTYPE_F32 ? pa::KV_F32 : pa::KV_I8;
+}
 
 // Persistent decode launch plan, cached per (device, variant, num_seqs).
 int cached_plan(int kv, int qbf, int D, int nt, int B, int tma, pa::DecodeLaunch* out) {
@@ -217,6 +225,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 bool make_pool_map(CUtensorMap* m, void* base, int dtype, int D, int H, int BS, int NB, long long s_head,
                    long long s_slot, long long s_blk) {
   auto enc = encode_fn();
+  if (dtype == PA_DTYPE_F32) return false;
   if (!enc || NB < 1 || BS < 8 || s_head <= 0 || s_slot <= 0 || s_blk <= 0) return false;
   const int elt = dtype == PA_DTYPE_I8 ? 1 : 2;
   const int rowb = D * elt;
@@ -267,6 +276,8 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
     return fail(PA_ERR_UNSUPPORTED, "decode kernel supports at most %d sequences per call", kMaxDecodeSeqs);
   if (p.maxq * p.G > kNcMax)
     return fail(PA_ERR_UNSUPPORTED, "decode kernel packs at most %d (q rows x group heads) columns", kNcMax);
+  if (kv->dtype == PA_DTYPE_F32)
+    return fail(PA_ERR_UNSUPPORTED, "the decode kernel reads fp16, bf16 or int8 pools (fp32 pools: paged_attn_forward)");
   if (p.B == 0 || p.maxq == 0) return PA_OK;
   const int nt = decode_nt(p);
   const int kv_k = kv_kind(kv->dtype);
@@ -442,7 +453,7 @@ int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   pa::AttnParams p;
   int rc = build_attn(io, kv, pg, nullptr, p);
   if (rc) return rc;
-  if (!use_decode(p) || p.B == 0 || p.maxq == 0) return PA_OK;
+  if (!use_decode(p, kv) || p.B == 0 || p.maxq == 0) return PA_OK;
   pa::KvMaps maps;
   const bool tma = make_kv_maps(kv, &maps);
   pa::DecodeLaunch plan;
@@ -458,7 +469,7 @@ int paged_attn_forward(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa
   pa::AttnParams p;
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
-  if (use_decode(p)) return run_decode(p, kv, workspace, workspace_bytes, stream);
+  if (use_decode(p, kv)) return run_decode(p, kv, workspace, workspace_bytes, stream);
   return run_prefill(p, kv, io, stream);
 }
 
@@ -500,7 +511,7 @@ int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
   if (total_q_rows == 0) return PA_OK;
   p.q_start = q_start;
   p.q_total = total_q_rows;
-  if (use_decode(p)) return run_decode(p, kv, workspace, workspace_bytes, stream);
+  if (use_decode(p, kv)) return run_decode(p, kv, workspace, workspace_bytes, stream);
   return run_prefill(p, kv, io, stream);
 }
 
@@ -558,7 +569,7 @@ int paged_attn_decode_peers(const pa_attn_io_t* io, const pa_kv_cache_t* kv, con
     p.o_peer[r] = o_peers[r];
   }
   p.n_peers = n_peers;
-  if (!use_decode(p))
+  if (!use_decode(p, kv))
     return fail(PA_ERR_UNSUPPORTED, "decode_peers: max_q_len * (num_q_heads / num_kv_heads) must be <= %d", kNcMax);
   return run_decode(p, kv, workspace, workspace_bytes, stream);
 }
@@ -624,6 +635,8 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
     return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc) supports at most %d sequences per call", kMaxDecodeSeqs);
   if (p.maxq * p.G > kNcMax)
     return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc) packs at most %d (q rows x group heads) columns", kNcMax);
+  if (kv->dtype == PA_DTYPE_F32)
+    return fail(PA_ERR_UNSUPPORTED, "decode (no-alloc) reads fp16, bf16 or int8 pools");
   if (p.B == 0 || p.maxq == 0) return PA_OK;
   void* scratch = nullptr;
   rc = static_scratch_address(&scratch);

@@ -1049,8 +1049,11 @@ int decode_plan(int kv_kind, int q_bf16, int D, int nt, int B, int use_tma, Deco
 
 namespace {
 // One CTA: thread t posts `epoch` into slot `rank` of peer t's flags, then
-// waits for slot t of this GPU's flags to hold `epoch` (system-scope
+// waits for slot t of this GPU's flags to reach `epoch` (system-scope
 // release / acquire; each wait gives up after ~0.4 s with a status bit).
+// A peer can pass this barrier as soon as this GPU has posted, run its next
+// step and post epoch + 1 before this GPU has read the slot, so any value at
+// or past `epoch` ends the wait (a peer is never more than one epoch ahead).
 __global__ void __launch_bounds__(32) pa_peer_barrier_kernel(int* local_flags, const PeerFlags peers, int n,
                                                               int rank, int epoch, int* status) {
   pdl_enter();
@@ -1065,7 +1068,7 @@ __global__ void __launch_bounds__(32) pa_peer_barrier_kernel(int* local_flags, c
     for (int i = 0; i < (1 << 22); ++i) {
       int v;
       asm volatile("ld.acquire.sys.global.b32 %0, [%1];\n" : "=r"(v) : "l"(local_flags + t) : "memory");
-      if (v == epoch) {
+      if (v - epoch >= 0) {  // epochs only grow; a peer may already have posted the next one
         ok = true;
         break;
       }

@@ -255,6 +255,22 @@ __global__ void __launch_bounds__(PA_WRITE_THREADS, PA_WRITE_MINB) kv_write_kern
     }
     return;
   }
+  if (p.cache_dtype == PA_DTYPE_F32) {
+#pragma unroll
+    for (int it = 0; it < C::NL; ++it) {
+      const int j = it * C::RPI + sub;
+      const int h = h0 + (j >> 1);
+      if (h >= p.Hkv) continue;
+      const bool isv = j & 1;
+      float* dst = static_cast<float*>(isv ? p.v : p.k) + (isv ? vb + h * p.v_shead : kb + h * p.k_shead) + part * EPL;
+      float f[EPL];
+      unpack_row<IN, EPL>(raw[it], f);
+#pragma unroll
+      for (int i = 0; i < EPL / 4; ++i)
+        reinterpret_cast<float4*>(dst)[i] = make_float4(f[4 * i], f[4 * i + 1], f[4 * i + 2], f[4 * i + 3]);
+    }
+    return;
+  }
   const bool bf = p.cache_dtype == PA_DTYPE_BF16;
 #pragma unroll
   for (int it = 0; it < C::NL; ++it) {

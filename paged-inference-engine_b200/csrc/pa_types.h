@@ -11,7 +11,7 @@
 namespace pa {
 
 // Element types of the KV pool / Q operand (kernel template tags).
-enum : int { KV_F16 = 0, KV_BF16 = 1, KV_I8 = 2 };
+enum : int { KV_F16 = 0, KV_BF16 = 1, KV_I8 = 2, KV_F32 = 3 };
 enum : int { Q_F16 = 0, Q_BF16 = 1 };
 
 // Device-side status bits (OR-ed into the optional status word).

@@ -14,6 +14,12 @@
 // thread dequantises its share (q * scale in fp32, rounded once to the MMA
 // type) into a 16-bit tile, the same value the reference forms before its
 // dot product (kernels/flash_attention.py:83-84).
+//
+// FP32 pools (the reference kernel casts any float pool to fp32,
+// kernels/flash_attention.py:79-84, and its tl.dot then runs in TF32 on the
+// GPU): the fp32 tile is staged and rounded once to fp16, whose 11-bit
+// significand equals TF32's, before the fp16 MMAs.  Values must lie inside
+// the fp16 range (|x| < 65520); beyond it the rounding overflows to inf.
 #include "pa_common.cuh"
 
 namespace pa {
@@ -42,16 +48,19 @@ __device__ __forceinline__ int pf_seq_keys(const AttnParams& p, int b) {
 template <int D, int KVT>
 struct PfCfg {
   static constexpr bool INT8 = KVT == KV_I8;
+  static constexpr bool F32 = KVT == KV_F32;
+  static constexpr bool CONV = INT8 || F32;  // staged tiles converted to 16-bit operands
+  static constexpr int ELT = INT8 ? 1 : F32 ? 4 : 2;
   static constexpr int ROWB = D * 2;  // 16-bit operand rows
   static constexpr int CH = ROWB / 16;
   static constexpr int TB = PF_BN * ROWB;
   static constexpr int QB = PF_BM * ROWB;
-  static constexpr int RAWROWB = INT8 ? D : ROWB;
+  static constexpr int RAWROWB = D * ELT;
   static constexpr int RAWCH = RAWROWB / 16;
   static constexpr int RAWTB = PF_BN * RAWROWB;
   static constexpr int SCB = INT8 ? (2 * PF_BN * 4 + 32) : 0;  // K/V scale words + 4 mask words (+pad)
   static constexpr int STAGEB = 2 * RAWTB + SCB;
-  static constexpr int CONVB = INT8 ? 2 * TB : 0;
+  static constexpr int CONVB = CONV ? 2 * TB : 0;
   static constexpr int SMEM = QB + 2 * STAGEB + CONVB;
 };
 
@@ -61,7 +70,7 @@ template <int D, int KVT>
 __device__ __forceinline__ void pf_load_kv(const AttnParams& p, const int* bt_row, int nkeys, int kvh, int k0,
                                            unsigned char* st, int tid) {
   using C = PfCfg<D, KVT>;
-  constexpr int ELT = C::INT8 ? 1 : 2;
+  constexpr int ELT = C::ELT;
   constexpr int TOTAL = PF_BN * C::RAWCH;
   const char* kbase = static_cast<const char*>(p.k);
   const char* vbase = static_cast<const char*>(p.v);
@@ -89,7 +98,7 @@ __device__ __forceinline__ void pf_load_kv(const AttnParams& p, const int* bt_ro
       ksrc = kbase + (blk * p.k_sblk + slot * p.k_sslot + kvh * p.k_shead) * ELT + ch * 16;
       vsrc = vbase + (blk * p.v_sblk + slot * p.v_sslot + kvh * p.v_shead) * ELT + ch * 16;
     }
-    const int pc = C::INT8 ? ch : swz16(row, ch);
+    const int pc = C::CONV ? ch : swz16(row, ch);
     cp_async_16(sk + row * C::RAWROWB + pc * 16, ksrc, ok ? 16 : 0);
     cp_async_16(sv + row * C::RAWROWB + pc * 16, vsrc, ok ? 16 : 0);
   }
@@ -151,6 +160,28 @@ __device__ __forceinline__ void pf_convert(const unsigned char* st, unsigned cha
     unsigned char* dst = conv + isv * C::TB + row * C::ROWB;
     *reinterpret_cast<uint4*>(dst + swz16(row, 2 * ch) * 16) = make_uint4(out[0], out[1], out[2], out[3]);
     *reinterpret_cast<uint4*>(dst + swz16(row, 2 * ch + 1) * 16) = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
+
+// FP32 stage -> 16-bit tiles (K and V), swizzled for ldmatrix: each thread
+// turns two 16-byte chunks of fp32 (8 values) into one chunk of fp16.
+template <int D>
+__device__ __forceinline__ void pf_convert_f32(const unsigned char* st, unsigned char* conv, int tid) {
+  using C = PfCfg<D, KV_F32>;
+  constexpr int TOTAL = 2 * PF_BN * C::CH;  // 16-bit output chunks over K and V
+#pragma unroll
+  for (int it = 0; it < TOTAL / PF_THREADS; ++it) {
+    const int c = it * PF_THREADS + tid;
+    const int isv = c / (PF_BN * C::CH);
+    const int cc = c % (PF_BN * C::CH);
+    const int row = cc / C::CH;
+    const int ch = cc % C::CH;
+    const float4* src = reinterpret_cast<const float4*>(st + isv * C::RAWTB + row * C::RAWROWB + ch * 32);
+    const float4 a = src[0];
+    const float4 b = src[1];
+    unsigned char* dst = conv + isv * C::TB + row * C::ROWB;
+    *reinterpret_cast<uint4*>(dst + swz16(row, ch) * 16) =
+        make_uint4(pack2<false>(a.x, a.y), pack2<false>(a.z, a.w), pack2<false>(b.x, b.y), pack2<false>(b.z, b.w));
   }
 }
 
@@ -246,8 +277,9 @@ __global__ void __launch_bounds__(PF_THREADS) pa_prefill_kernel(const AttnParams
     const unsigned char* st = stage0 + (t & 1) * C::STAGEB;
     const unsigned char* kt;
     const unsigned char* vt;
-    if constexpr (INT8) {
-      pf_convert<D, MB>(st, conv, p.scale_f32, tid);
+    if constexpr (C::CONV) {
+      if constexpr (INT8) pf_convert<D, MB>(st, conv, p.scale_f32, tid);
+      else pf_convert_f32<D>(st, conv, tid);
       __syncthreads();
       kt = conv;
       vt = conv + C::TB;
@@ -391,6 +423,7 @@ cudaError_t pf_dispatch(const AttnParams& p, int kv, cudaStream_t s) {
   const bool qbf = p.q_bf16 != 0;
   if (kv == KV_F16) return qbf ? pf_launch<D, KV_F16, Q_BF16>(p, s) : pf_launch<D, KV_F16, Q_F16>(p, s);
   if (kv == KV_BF16) return qbf ? pf_launch<D, KV_BF16, Q_BF16>(p, s) : pf_launch<D, KV_BF16, Q_F16>(p, s);
+  if (kv == KV_F32) return qbf ? pf_launch<D, KV_F32, Q_BF16>(p, s) : pf_launch<D, KV_F32, Q_F16>(p, s);
   return qbf ? pf_launch<D, KV_I8, Q_BF16>(p, s) : pf_launch<D, KV_I8, Q_F16>(p, s);
 }
 

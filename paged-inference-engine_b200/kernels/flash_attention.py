@@ -22,6 +22,14 @@ backward compatible:
 * the causal mask is bottom-right aligned (decode query attends to its whole
   prefix); ``causal_top_left=True`` reproduces the reference's mask (:97);
 * GQA: ``H_kv = K.shape[2]`` may divide ``H``;
+* a pool in the reference model's own layout ``[NB, H, BS, D]``
+  (transformer/model.py:64-65, passed unchanged at :156-160) is recognised by
+  its dims (dim 1 is not ``block_size``, dim 2 is) and read as such; the
+  reference launcher would read it as ``[block, slot, head, d]`` and address
+  slots through the head stride;
+* float32 pools are rounded to float16 operands in the kernel (the
+  precision of the reference's TF32 ``tl.dot``; values must stay below
+  65520 in magnitude); float32 ``Q`` is rounded to the pool's 16-bit type;
 * scales may be per block ``[NB, H]`` (reference) or per token ``[NB, BS, H]``;
   they are applied for INT8 pools and ignored for float16 / bfloat16 pools
   (pass ``None``);

@@ -48,8 +48,8 @@ def kv_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: Optiona
     if k_cache.shape != v_cache.shape or k_cache.dtype != v_cache.dtype:
         raise ValueError(f"K and V pools differ: {tuple(k_cache.shape)}/{k_cache.dtype} vs "
                          f"{tuple(v_cache.shape)}/{v_cache.dtype}")
-    if k_cache.dtype not in (torch.float16, torch.bfloat16, torch.int8):
-        raise ValueError(f"KV pool dtype {k_cache.dtype} unsupported (float16, bfloat16 or int8)")
+    if k_cache.dtype not in (torch.float16, torch.bfloat16, torch.int8, torch.float32):
+        raise ValueError(f"KV pool dtype {k_cache.dtype} unsupported (float16, bfloat16, int8 or float32)")
     if k_cache.stride(3) != 1 or v_cache.stride(3) != 1:
         raise ValueError("KV pools need a contiguous head_dim")
     nb, bs, h, d = k_cache.shape
@@ -89,6 +89,22 @@ def _scale_strides(s: torch.Tensor, nb: int, bs: int, h: int) -> tuple[int, int,
             raise ValueError(f"per-token scales must be [{nb}, {bs}, {h}], got {tuple(s.shape)}")
         return s.stride(0), s.stride(1), s.stride(2)
     raise ValueError("scales must be 2-D [NB, H] or 3-D [NB, BS, H]")
+
+
+def pool_layout(K: torch.Tensor, V: torch.Tensor, block_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The pools as [block, slot, head, d] views.
+
+    The reference launcher reads dims 1 and 2 as (slot, head)
+    (kernels/flash_attention.py:158-159) while the reference model allocates
+    its caches as [num_blocks, heads, block_size, d_k]
+    (transformer/model.py:64-65) and passes them unchanged
+    (transformer/model.py:156-160).  A pool whose dim 1 is not ``block_size``
+    but whose dim 2 is can only be the model's layout, so it is read through
+    the transposed view; a pool that fits the launcher's layout is read as is.
+    """
+    if K.dim() == 4 and K.shape[1] != block_size and K.shape[2] == block_size:
+        return K.transpose(1, 2), V.transpose(1, 2)
+    return K, V
 
 
 def paging_desc(block_table: torch.Tensor, num_blocks: torch.Tensor, q_len: torch.Tensor,
@@ -136,6 +152,13 @@ def status_word(device: torch.device) -> torch.Tensor:
 def _raise_status(fn: str, st: torch.Tensor) -> None:
     v = int(st.item())
     if v:
+        st.zero_()
+        _raise_status_value(fn, v)
+
+
+def _raise_status_value(fn: str, v: int) -> None:
+    """Raise IndexError naming the bits of a nonzero device status word."""
+    if v:
         bits = []
         if v & _lib.PA_STATUS_BAD_BLOCK_ID:
             bits.append("block id outside the pool")
@@ -147,7 +170,6 @@ def _raise_status(fn: str, st: torch.Tensor) -> None:
             bits.append("sequence index outside the block table")
         if v & _lib.PA_STATUS_PEER_TIMEOUT:
             bits.append("a peer GPU never reached the output-exchange barrier")
-        st.zero_()
         raise IndexError(f"{fn}: device status {v:#x}: " + "; ".join(bits))
 
 
@@ -162,6 +184,7 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
     if Q.dim() != 4:
         raise ValueError("Q must be [num_seqs, num_q_heads, max_q_len, head_dim]")
     B, Hq, maxq, D = Q.shape
+    K, V = pool_layout(K, V, block_size)
     if K.shape[1] != block_size:
         raise ValueError(f"block_size {block_size} does not match the pool's slot dimension {K.shape[1]}")
     if K.shape[3] != D:
@@ -238,6 +261,7 @@ def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch
     B = block_table.shape[0]
     if cu_seqlens_q.dim() != 1 or cu_seqlens_q.shape[0] != B + 1:
         raise ValueError(f"cu_seqlens_q must hold {B + 1} offsets for {B} sequences")
+    K, V = pool_layout(K, V, block_size)
     if K.shape[1] != block_size:
         raise ValueError(f"block_size {block_size} does not match the pool's slot dimension {K.shape[1]}")
     if K.shape[3] != D:

@@ -47,6 +47,13 @@ class PeerOutputExchange:
         self.group, self.world, self.rank, self.device = group, world, rank, device
         self.shape = None
         self.epoch = 0
+        # Device status word shared by the decode kernels and the barrier of every
+        # step; after each step it is copied into a pinned host slot of that step's
+        # buffer parity, and read back two steps later (when the buffer comes round
+        # again), so a peer that missed the barrier raises without a per-step sync.
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._host_status = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+        self._events: list = [None, None]
 
     def ensure(self, shape: tuple[int, ...]) -> None:
         if self.shape == tuple(shape):
@@ -89,6 +96,8 @@ class PeerOutputExchange:
 
         lib = _lib.load()
         torch.cuda.synchronize(self.device)
+        pending = [int(self._host_status[k]) for k in (0, 1) if self._events[k] is not None]
+        self._events = [None, None]
         dist.barrier(group=self.group)  # no peer still writes into this rank's buffers
         with torch.cuda.device(self.device):
             for k in range(3):
@@ -99,24 +108,58 @@ class PeerOutputExchange:
             for k in range(3):
                 _lib.check("paged_attn_peer_free", lib.paged_attn_peer_free(self.local[k]))
         self.shape, self.views = None, None
+        bad = [v for v in pending if v]
+        if bad:
+            from . import ops
 
-    def exchange(self, run_decode: Callable[[torch.Tensor, list[int]], None], head_lo: int, head_hi: int,
-                 status: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """run_decode(out_view, peer_ptrs) writes heads [head_lo, head_hi) into every rank; returns all heads."""
+            ops._raise_status_value("peer output exchange", bad[0])
+
+    def check(self, parity: Optional[int] = None) -> None:
+        """Raise if a finished step (both parities, or one) reported a device error.
+
+        Waits for that step's status copy; a step still in flight is waited for.
+        """
+        from . import ops
+
+        for k in ((0, 1) if parity is None else (parity,)):
+            ev = self._events[k]
+            if ev is None:
+                continue
+            ev.synchronize()
+            self._events[k] = None
+            v = int(self._host_status[k])
+            if v:
+                self.status.zero_()
+                self._host_status.zero_()
+                ops._raise_status_value("peer output exchange", v)
+
+    def exchange(self, run_decode: Callable[[torch.Tensor, list[int], torch.Tensor], None], head_lo: int,
+                 head_hi: int) -> torch.Tensor:
+        """run_decode(out_view, peer_ptrs, status) writes heads [head_lo, head_hi) into every rank.
+
+        Returns the buffer holding all heads.  Raises IndexError (naming the
+        status bits) when the step that last used the same buffer reported a
+        device error: a peer that never reached the barrier (its heads are then
+        missing) or bad paging metadata.
+        """
         from . import _lib
 
         lib = _lib.load()
         k = self.epoch & 1
+        self.check(k)  # the step two back used this buffer: its status must be clean
         self.epoch += 1
         full = self.views[k]
         view = full[:, head_lo:head_hi]
         off = view.data_ptr() - full.data_ptr()
-        run_decode(view, [p + off for p in self.peers[k]])
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        st = None if status is None else status.data_ptr()
+        run_decode(view, [p + off for p in self.peers[k]], self.status)
+        stream = torch.cuda.current_stream(self.device)
         _lib.check("paged_attn_peer_barrier",
-                   lib.paged_attn_peer_barrier(self.local[2], self.flags, self.world, self.rank, self.epoch, st,
-                                               stream))
+                   lib.paged_attn_peer_barrier(self.local[2], self.flags, self.world, self.rank, self.epoch,
+                                               self.status.data_ptr(), stream.cuda_stream))
+        self._host_status[k:k + 1].copy_(self.status, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._events[k] = ev
         return full
 
 
@@ -133,7 +176,10 @@ class KVHeadShardedDecoder:
     output row into every rank's mapped output buffer and a cross-GPU flag
     barrier ends the step.  The returned tensor is then one of two buffers the
     steps alternate between: consume it on the current stream before the
-    next-but-one ``forward``.
+    next-but-one ``forward``.  Each step's device status (a peer that never
+    reached the barrier, bad paging metadata) is read back two steps later,
+    when its buffer comes round again, and raised there; ``check()`` reads the
+    outstanding ones.
     """
 
     def __init__(self, num_q_heads: int, num_kv_heads: int, head_dim: int, group=None,
@@ -155,6 +201,15 @@ class KVHeadShardedDecoder:
             attention_fn = flash_attention_forward
         self.attention_fn = attention_fn
         self._gather_buf = None
+
+    def check(self) -> None:
+        """Wait for the outstanding peer-exchange steps and raise if one reported a device error.
+
+        ``forward`` checks each step two steps later on its own; call this after
+        the last step whose output is used.
+        """
+        if self._peer is not None:
+            self._peer.check()
 
     def close(self) -> None:
         """Release the peer-exchange buffers (collective; a no-op for the NCCL exchange)."""
@@ -186,9 +241,9 @@ class KVHeadShardedDecoder:
             self._peer = PeerOutputExchange(self.group, self.world, self.rank, Q_local.device)
         self._peer.ensure((B, self.Hq, q, D))
 
-        def run(view, ptrs):
+        def run(view, ptrs, status):
             ops.paged_attention_peers(Q_local, K, V, q_len, block_table, num_blocks, int(block_size), kv_len,
-                                      k_scale, v_scale, view, ptrs)
+                                      k_scale, v_scale, view, ptrs, status=status)
 
         return self._peer.exchange(run, self.q_lo, self.q_hi)
 

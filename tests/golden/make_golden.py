@@ -21,7 +21,19 @@ GQA.  INT8 per-token cases feed the reference kernel the dequantised pool
 (int8 * scale, float32) with unit scales, which is the arithmetic of its
 dequantise step (:83-84).
 
-Usage:  python tests/golden/make_golden.py
+* ``model_layer_steps.npz`` -- three steps of the reference's own
+  ``MultiHeadAttention.forward`` (transformer/model.py:69-173) driven by its
+  own Scheduler and BlockManager (core/scheduler.py, core/block_manager.py)
+  with the step metadata built as core/model_runner.py:66-107 builds it.  The
+  layer's call of ``FlashAttentionFunction.apply`` is captured (its exact
+  arguments: float32 Q, the model's [num_blocks, heads, block_size, d_k] INT8
+  pools with float32 per-block scales) and answered by the oracle reading the
+  pools in the model's own layout (bottom-right mask); the layer output after
+  W_o is recorded too.
+
+Usage:  python tests/golden/make_golden.py [--ref PATH] [case ...]
+        (PATH defaults to $PIE_REFERENCE_ROOT; with no case every fixture is
+        regenerated)
 """
 from __future__ import annotations
 
@@ -34,7 +46,19 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = "/root/reference"
+def _ref_root() -> str:
+    if "--ref" in sys.argv:
+        i = sys.argv.index("--ref")
+        root = sys.argv[i + 1]
+        del sys.argv[i:i + 2]
+        return root
+    root = os.environ.get("PIE_REFERENCE_ROOT")
+    if not root:
+        sys.exit("make_golden.py: pass --ref PATH or set PIE_REFERENCE_ROOT to the reference checkout")
+    return root
+
+
+REF = os.path.abspath(_ref_root())
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REF)
 sys.path.insert(0, os.path.dirname(os.path.dirname(OUT)))
@@ -280,14 +304,116 @@ def case_quant():
     print("quant", s1, s3)
 
 
+def step_metadata(prefill_seqs, decode_seqs):
+    """The per-step lists core/model_runner.py:66-107 builds (its F6 decode position included)."""
+    sequence_id, length, offset, position_ids, pos_seq_id, kv_len = [], [], [], [], [], []
+    cnt = 0
+    for seq in prefill_seqs:
+        n = len(seq.prompt_token_ids)
+        sequence_id.append(seq.seq_id)
+        length.append(n)
+        offset.append(cnt)
+        cnt += n
+        pos_seq_id.extend([seq.seq_id] * n)
+        position_ids.extend(range(len(seq.token_ids)))
+        kv_len.append(n)
+    for seq in decode_seqs:
+        sequence_id.append(seq.seq_id)
+        length.append(1)
+        offset.append(cnt)
+        cnt += 1
+        pos_seq_id.append(seq.seq_id)
+        position_ids.append(len(seq.token_ids))
+        kv_len.append(len(seq.token_ids) + 1)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32)  # noqa: E731
+    return dict(sequence_id=i32(sequence_id), length=i32(length), offset=i32(offset),
+                position_ids=i32(position_ids), pos_seq_id=i32(pos_seq_id), kv_len=i32(kv_len))
+
+
+def case_model_layer():
+    """The reference attention layer's own call of the kernel, captured over three scheduler steps."""
+    import core.config as core_config
+
+    # the layer sizes its pools from this dict at construction: a small pool
+    core_config.core_configurations.update(block_size=16, num_blocks=24)
+    import transformer.model as tm
+    from core.block_manager import BlockManager
+    from core.scheduler import Scheduler
+    from core.sequence import Sequence
+
+    assert tm.__file__.startswith(REF), tm.__file__
+    torch.manual_seed(21)
+    d_model, heads, BS = 128, 2, 16
+    layer = tm.MultiHeadAttention(d_model, heads).eval()
+    bm = BlockManager(24, BS)
+    sched = Scheduler(bm, BS, 100, skip_threshold=3, lookahead=5)
+    gen = torch.Generator().manual_seed(22)
+    prompts = [[int(t) for t in torch.randint(0, 1000, (n,), generator=gen)] for n in (20, 7, 33)]
+    for i, pr in enumerate(prompts):
+        sched.add_request(Sequence(seq_id=i, prompt_token_ids=pr))
+
+    captured = []
+
+    class Capture:
+        """Stands in for FlashAttentionFunction: records the call, answers with the oracle."""
+
+        @staticmethod
+        def apply(Q, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale, v_scale):
+            Kn = K.numpy().transpose(0, 2, 1, 3)  # the model writes [block, head, slot, d]
+            Vn = V.numpy().transpose(0, 2, 1, 3)
+            O, L = orc.paged_attention(Q.numpy(), Kn, Vn, q_len.numpy(), block_table.numpy(), num_blocks.numpy(),
+                                       int(block_size), kv_len.numpy(), k_scale.numpy(), v_scale.numpy())
+            captured.append(dict(Q=Q.clone().numpy(), K=K.clone().numpy(), V=V.clone().numpy(),
+                                 q_len=q_len.clone().numpy(), block_table=block_table.clone().numpy(),
+                                 num_blocks=num_blocks.clone().numpy(), kv_len=kv_len.clone().numpy(),
+                                 k_scale=k_scale.clone().numpy(), v_scale=v_scale.clone().numpy(), O_ref=O,
+                                 block_size=np.int32(block_size)))
+            return torch.from_numpy(O).to(torch.float16)
+
+    tm.FlashAttentionFunction = Capture
+    out = {}
+    for step in range(3):
+        if step == 2:
+            sched.add_request(Sequence(seq_id=3, prompt_token_ids=[5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16]))
+        so = sched.schedule()
+        md = step_metadata(so.prefill_seqs, so.decode_seqs)
+        T = int(md["length"].sum())
+        x = torch.randn(T, d_model, generator=gen)
+        with torch.no_grad():
+            y = layer(x, x, x, bm.block_table, md["length"], md["kv_len"], md["sequence_id"], md["offset"],
+                      md["length"], md["position_ids"], md["pos_seq_id"])
+        c = captured[-1]
+        for k, v in c.items():
+            out[f"s{step}_{k}"] = v
+        out[f"s{step}_y"] = y.numpy()
+        out[f"s{step}_offset"] = md["offset"].numpy()
+        out[f"s{step}_length"] = md["length"].numpy()
+        for seq in so.prefill_seqs + so.decode_seqs:  # core/model_runner.py:140-155, no EOS
+            seq.token_ids.append(int(torch.randint(0, 1000, (1,), generator=gen)))
+        print(f"model_layer step {step}: {len(so.prefill_seqs)} prefill, {len(so.decode_seqs)} decode, "
+              f"max|O| {np.abs(c['O_ref']).max():.3f}")
+    out["W_o"] = layer.W_o.weight.detach().numpy()
+    out["b_o"] = layer.W_o.bias.detach().numpy()
+    out["steps"] = np.int32(3)
+    np.savez_compressed(os.path.join(OUT, "model_layer_steps.npz"), **out)
+
+
+CASES = {
+    "quant": case_quant,
+    "reference_test": case_reference_test,
+    "cfg1_fp32": lambda: case_cfg1("fp32"),
+    "cfg1_int8_block": lambda: case_cfg1("int8_block"),
+    "cfg1_int8_token": lambda: case_cfg1("int8_token"),
+    "gqa_decode_d128": lambda: case_gqa("gqa_decode_d128", 8, 2, 128, 16, [37, 128, 200, 16, 1], [1, 1, 1, 1, 1],
+                                        False, 11),
+    "gqa_chunked_d64": lambda: case_gqa("gqa_chunked_d64", 8, 2, 64, 16, [40, 70, 16], [3, 16, 16], False, 12),
+    "gqa_int8_token_d128": lambda: case_gqa("gqa_int8_token_d128", 8, 2, 128, 16, [50, 97, 130], [1, 1, 1], True,
+                                            13),
+    "gqa_int8_chunked_bs32": lambda: case_gqa("gqa_int8_chunked_bs32", 4, 1, 128, 32, [65, 90], [7, 33], True, 14),
+    "top_left": case_top_left,
+    "model_layer": case_model_layer,
+}
+
 if __name__ == "__main__":
-    case_quant()
-    case_reference_test()
-    case_cfg1("fp32")
-    case_cfg1("int8_block")
-    case_cfg1("int8_token")
-    case_gqa("gqa_decode_d128", 8, 2, 128, 16, [37, 128, 200, 16, 1], [1, 1, 1, 1, 1], False, 11)
-    case_gqa("gqa_chunked_d64", 8, 2, 64, 16, [40, 70, 16], [3, 16, 16], False, 12)
-    case_gqa("gqa_int8_token_d128", 8, 2, 128, 16, [50, 97, 130], [1, 1, 1], True, 13)
-    case_gqa("gqa_int8_chunked_bs32", 4, 1, 128, 32, [65, 90], [7, 33], True, 14)
-    case_top_left()
+    for name in (sys.argv[1:] or list(CASES)):
+        CASES[name]()

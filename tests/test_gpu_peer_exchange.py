@@ -63,3 +63,65 @@ def _rank(rank, world, port):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one box")
 def test_peer_exchange_matches_all_gather():
     mp.spawn(_rank, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _barrier(flags_local, flag_ptrs, n, rank, epoch, status):
+    import ctypes
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "paged-inference-engine_b200"))
+    from pie_b200 import _lib
+
+    lib = _lib.load()
+    peers = (ctypes.c_void_p * n)(*flag_ptrs)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check("paged_attn_peer_barrier",
+               lib.paged_attn_peer_barrier(flags_local.data_ptr(), peers, n, rank, epoch, status.data_ptr(), stream))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_peer_barrier_gives_up_on_a_silent_peer():
+    """One GPU, two ranks' worth of flags: peer 1's slot is a local array nobody posts to.
+
+    The bounded wait must run out, set the peer-timeout status bit and return
+    (the context stays usable); rank 0's own post still lands in both arrays.
+    """
+    import time
+
+    from pie_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    local = torch.zeros(64, dtype=torch.int32, device=dev)
+    silent = torch.zeros(64, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    _barrier(local, [local.data_ptr(), silent.data_ptr()], 2, 0, 1, status)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert int(status.item()) & _lib.PA_STATUS_PEER_TIMEOUT, "the wait on the silent peer did not report a timeout"
+    assert dt < 20.0, f"bounded wait took {dt:.1f} s"
+    assert int(local[0].item()) == 1 and int(silent[0].item()) == 1, "rank 0 did not post its epoch"
+    # the context is still usable
+    x = torch.arange(10, device=dev).sum()
+    assert int(x.item()) == 45
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_peer_barrier_accepts_a_peer_one_epoch_ahead():
+    """A peer that already passed this barrier and posted the next epoch ends the wait at once."""
+    from pie_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    local = torch.zeros(64, dtype=torch.int32, device=dev)
+    peer = torch.zeros(64, dtype=torch.int32, device=dev)
+    local[1] = 6  # peer 1 has posted epoch 6 into this rank's slot 1
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _barrier(local, [local.data_ptr(), peer.data_ptr()], 2, 0, 5, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert int(local[0].item()) == 5 and int(peer[0].item()) == 5
+    assert int(status.item()) & _lib.PA_STATUS_PEER_TIMEOUT == 0

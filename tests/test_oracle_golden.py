@@ -114,3 +114,30 @@ def test_oracle_edge_cases():
     assert not O[0].any() and np.isneginf(L[0]).all()      # q_len 0
     assert not O[2].any() and np.isneginf(L[2, :, :4]).all()  # num_blocks 0 -> no keys
     assert np.isfinite(L[1, :, :2]).all()
+
+
+def test_model_layer_fixture_is_consistent():
+    """model_layer_steps.npz: the captured calls answer to the oracle and the recorded layer outputs.
+
+    The fixture holds the reference layer's own arguments (float32 Q, INT8
+    pools in the model's [NB, H, BS, D] layout, float32 per-block scales); the
+    oracle on the model layout reproduces O, and W_o over the unpadded float16
+    O reproduces the layer output the reference computed.
+    """
+    g = load_golden("model_layer_steps.npz")
+    for s in range(int(g["steps"])):
+        a = {k[len(f"s{s}_"):]: v for k, v in g.items() if k.startswith(f"s{s}_")}
+        assert a["Q"].dtype == np.float32 and a["K"].dtype == np.int8 and a["k_scale"].dtype == np.float32
+        NB, H, BS, D = a["K"].shape
+        assert BS == int(a["block_size"]) and H != BS
+        O, _ = orc.paged_attention(a["Q"], a["K"].transpose(0, 2, 1, 3), a["V"].transpose(0, 2, 1, 3), a["q_len"],
+                                   a["block_table"], a["num_blocks"], BS, a["kv_len"], a["k_scale"], a["v_scale"])
+        np.testing.assert_array_equal(O, a["O_ref"])
+        T = int(a["length"].sum())
+        O16 = O.astype(np.float16).astype(np.float32)
+        flat = np.zeros((T, H, D), np.float32)
+        for k in range(O.shape[0]):
+            st, n = int(a["offset"][k]), int(a["length"][k])
+            flat[st:st + n] = O16[k, :, :n].transpose(1, 0, 2)
+        y = flat.reshape(T, -1) @ g["W_o"].T + g["b_o"]
+        np.testing.assert_allclose(y, a["y"], atol=1e-4)
