@@ -309,6 +309,85 @@ int kv_write_quant(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_pagi
 int kv_write_copy(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
                   void* stream);
 
+/*
+ * Device-resident block pool: the free list and every sequence's block list
+ * kept in device memory and updated in place, replacing the host allocator
+ * and the per-step block-table rebuild of the reference:
+ *   core/block_manager.py:19-68    BlockManager (allocate / release_blocks)
+ *   transformer/model.py:126-152   num_blocks_per_seq + padded int32 table
+ *   core/model_runner.py:66-107    per-token positions / sequence rows
+ * All arrays are int32 device memory owned by the caller:
+ *   free_stack  [num_blocks]   free ids in [0, *free_top); the top is the end
+ *   free_top    [1]
+ *   table       [max_seqs, table_stride]  block ids of each sequence slot
+ *               (row width max_blocks_per_seq <= table_stride)
+ *   count       [max_seqs]     blocks of each slot, -1 = no entry
+ * A "slot" is the caller's small integer name for a live sequence (the
+ * reference keys its dict by seq_id; the host side maps seq_id -> slot).
+ */
+typedef struct {
+  int32_t* free_stack;
+  int32_t* free_top;
+  int32_t* table;
+  int32_t* count;
+  int64_t table_stride;
+  int32_t num_blocks;
+  int32_t max_seqs;
+  int32_t max_blocks_per_seq;
+  int32_t _reserved;
+} pa_block_pool_t;
+
+/* Operation kinds and per-operation results of block_pool_apply
+ * (results 0-2 are the values of the reference's AllocStatus,
+ * core/block_manager.py:9-12). */
+enum { PA_POOL_ALLOCATE = 0, PA_POOL_RELEASE = 1 };
+enum {
+  PA_POOL_SUCCESS = 0,
+  PA_POOL_INSUFFICIENT_SPACE = 1,
+  PA_POOL_FAILURE = 2,           /* release of a slot without an entry      */
+  PA_POOL_ROW_FULL = 3,          /* allocation past max_blocks_per_seq      */
+  PA_POOL_INVALID = 4            /* bad slot, negative count, unknown kind  */
+};
+
+/* Fill the free list with 0..num_blocks-1 (list(range(num_blocks)),
+ * core/block_manager.py:27) and mark every slot empty. */
+int block_pool_init(const pa_block_pool_t* pool, void* stream);
+
+/*
+ * Apply n_ops operations in order, ops int32 [n_ops][3] = (kind, slot, n):
+ *   PA_POOL_ALLOCATE  pop n ids off the end of the free list and append them
+ *                     to the slot's list (creating it), or leave everything
+ *                     unchanged with INSUFFICIENT_SPACE when fewer than n are
+ *                     free (BlockManager.allocate, core/block_manager.py:29-44)
+ *   PA_POOL_RELEASE   push the slot's ids back in list order and remove the
+ *                     entry, or FAILURE when the slot has none
+ *                     (BlockManager.release_blocks, :47-57)
+ * results (int32 [n_ops], device, may be NULL) receives each status.  One
+ * launch; ops and results are device pointers.
+ */
+int block_pool_apply(const pa_block_pool_t* pool, const int32_t* ops, int32_t n_ops, int32_t* results, void* stream);
+
+/*
+ * Per-step attention inputs of num_seqs sequences (device arrays):
+ *   seq_slot, q_len, kv_len  int32 [num_seqs]; cu_seqlens int32 [num_seqs + 1]
+ * writes
+ *   block_table  int32 [num_seqs, bt_cols] (row stride bt_stride): each row
+ *                the slot's block ids, zero-padded (transformer/model.py:145-152)
+ *   num_blocks   int32 [num_seqs]
+ *   positions    int32 [total_tokens]: token i of sequence k, at row
+ *                cu_seqlens[k] + i, sits at kv_len[k] - q_len[k] + i
+ *                (core/model_runner.py:84-85, 96-97); may be NULL
+ *   token_seq    int32 [total_tokens]: its row k of block_table (the
+ *                seq_index of kv_write_quant); may be NULL
+ * A slot without an entry gives an all-zero row and PA_STATUS_BAD_SEQ_INDEX;
+ * a slot with more than bt_cols blocks is truncated with
+ * PA_STATUS_BAD_NUM_BLOCKS.
+ */
+int block_pool_step(const pa_block_pool_t* pool, const int32_t* seq_slot, const int32_t* q_len, const int32_t* kv_len,
+                    const int32_t* cu_seqlens, int32_t num_seqs, int32_t* block_table, int64_t bt_stride,
+                    int32_t bt_cols, int32_t* num_blocks, int32_t* positions, int32_t* token_seq,
+                    int32_t total_tokens, int32_t* status, void* stream);
+
 /* Message for the last failing call on this thread ("" if none). */
 const char* paged_attn_error_string(void);
 

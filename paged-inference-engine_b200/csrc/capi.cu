@@ -671,6 +671,77 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   return PA_OK;
 }
 
+static int block_pool_check(const pa_block_pool_t* pool, pa::PoolParams& p) {
+  if (!pool) return fail(PA_ERR_INVALID, "block pool descriptor is NULL");
+  if (pool->num_blocks < 0 || pool->max_seqs < 0 || pool->max_blocks_per_seq < 0)
+    return fail(PA_ERR_INVALID, "block pool sizes must be non-negative");
+  if (pool->table_stride < pool->max_blocks_per_seq)
+    return fail(PA_ERR_INVALID, "table_stride %lld is narrower than max_blocks_per_seq %d",
+                static_cast<long long>(pool->table_stride), pool->max_blocks_per_seq);
+  if (!pool->free_stack || !pool->free_top || !pool->count || (!pool->table && pool->max_seqs > 0))
+    return fail(PA_ERR_INVALID, "block pool array pointer is NULL");
+  p.free_stack = pool->free_stack;
+  p.free_top = pool->free_top;
+  p.table = pool->table;
+  p.count = pool->count;
+  p.table_stride = pool->table_stride;
+  p.num_blocks = pool->num_blocks;
+  p.max_seqs = pool->max_seqs;
+  p.max_blocks_per_seq = pool->max_blocks_per_seq;
+  return PA_OK;
+}
+
+int block_pool_init(const pa_block_pool_t* pool, void* stream) {
+  g_err[0] = 0;
+  pa::PoolParams p;
+  int rc = block_pool_check(pool, p);
+  if (rc) return rc;
+  cudaError_t e = pa::launch_block_pool_init(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "block_pool_init launch");
+}
+
+int block_pool_apply(const pa_block_pool_t* pool, const int32_t* ops, int32_t n_ops, int32_t* results, void* stream) {
+  g_err[0] = 0;
+  pa::PoolParams p;
+  int rc = block_pool_check(pool, p);
+  if (rc) return rc;
+  if (n_ops < 0) return fail(PA_ERR_INVALID, "n_ops < 0");
+  if (n_ops > 0 && !ops) return fail(PA_ERR_INVALID, "ops is NULL");
+  cudaError_t e = pa::launch_block_pool_apply(p, ops, n_ops, results, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "block_pool_apply launch");
+}
+
+int block_pool_step(const pa_block_pool_t* pool, const int32_t* seq_slot, const int32_t* q_len, const int32_t* kv_len,
+                    const int32_t* cu_seqlens, int32_t num_seqs, int32_t* block_table, int64_t bt_stride,
+                    int32_t bt_cols, int32_t* num_blocks, int32_t* positions, int32_t* token_seq,
+                    int32_t total_tokens, int32_t* status, void* stream) {
+  g_err[0] = 0;
+  pa::PoolParams p;
+  int rc = block_pool_check(pool, p);
+  if (rc) return rc;
+  if (num_seqs < 0 || bt_cols < 0 || total_tokens < 0) return fail(PA_ERR_INVALID, "negative step size");
+  if (num_seqs == 0) return PA_OK;
+  if (!seq_slot || !q_len || !kv_len || !cu_seqlens || !num_blocks || (!block_table && bt_cols > 0))
+    return fail(PA_ERR_INVALID, "block_pool_step: NULL argument");
+  if (bt_cols > 0 && bt_stride < bt_cols) return fail(PA_ERR_INVALID, "bt_stride narrower than bt_cols");
+  pa::StepParams s{};
+  s.seq_slot = seq_slot;
+  s.q_len = q_len;
+  s.kv_len = kv_len;
+  s.cu_seqlens = cu_seqlens;
+  s.num_seqs = num_seqs;
+  s.block_table = block_table;
+  s.bt_stride = bt_stride;
+  s.bt_cols = bt_cols;
+  s.num_blocks = num_blocks;
+  s.positions = positions;
+  s.token_seq = token_seq;
+  s.total_tokens = total_tokens;
+  s.status = status;
+  cudaError_t e = pa::launch_block_pool_step(p, s, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "block_pool_step launch");
+}
+
 const char* paged_attn_error_string(void) { return g_err; }
 
 const char* paged_attn_version(void) { return "0.1.0"; }

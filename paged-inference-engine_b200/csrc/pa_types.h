@@ -107,6 +107,43 @@ struct WriteParams {
   int* status;
 };
 
+// Device-resident block pool (csrc/block_pool.cu).
+enum : int { POOL_ALLOC = 0, POOL_RELEASE = 1 };
+enum : int {
+  POOL_SUCCESS = PA_POOL_SUCCESS,
+  POOL_INSUFFICIENT_SPACE = PA_POOL_INSUFFICIENT_SPACE,
+  POOL_FAILURE = PA_POOL_FAILURE,
+  POOL_ROW_FULL = PA_POOL_ROW_FULL,
+  POOL_INVALID = PA_POOL_INVALID,
+};
+struct PoolParams {
+  int* free_stack;  // [num_blocks]; free ids at [0, *free_top), the top is the end
+  int* free_top;
+  int* table;       // [max_seqs, table_stride]: block ids of each sequence slot
+  int* count;       // [max_seqs]: blocks of each slot, -1 = no entry
+  long long table_stride;
+  int num_blocks, max_seqs, max_blocks_per_seq;
+};
+struct StepParams {
+  const int* seq_slot;   // [num_seqs] pool slot of each step sequence
+  const int* q_len;      // [num_seqs]
+  const int* kv_len;     // [num_seqs]
+  const int* cu_seqlens; // [num_seqs + 1] first query row of each sequence
+  int num_seqs;
+  int* block_table;      // [num_seqs, bt_cols] out (row stride bt_stride)
+  long long bt_stride;
+  int bt_cols;
+  int* num_blocks;       // [num_seqs] out
+  int* positions;        // [total_tokens] out (may be NULL)
+  int* token_seq;        // [total_tokens] out (may be NULL)
+  int total_tokens;
+  int* status;
+};
+cudaError_t launch_block_pool_init(const PoolParams& p, cudaStream_t stream);
+cudaError_t launch_block_pool_apply(const PoolParams& p, const int* ops, int n_ops, int* results,
+                                    cudaStream_t stream);
+cudaError_t launch_block_pool_step(const PoolParams& p, const StepParams& s, cudaStream_t stream);
+
 // Launchers implemented in the kernel translation units.
 cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream);
 // Decode: persistent grid size (CTAs) for a configuration on the current

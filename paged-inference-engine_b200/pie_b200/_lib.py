@@ -114,6 +114,10 @@ SIGNATURES = {
                                       _vp, _vp]),
     "kv_write_copy": (ctypes.c_int, [ctypes.POINTER(PaKvNew), ctypes.POINTER(PaKvCache), ctypes.POINTER(PaPaging),
                                      _vp, _vp]),
+    "block_pool_init": (ctypes.c_int, [_vp, _vp]),
+    "block_pool_apply": (ctypes.c_int, [_vp, _vp, ctypes.c_int32, _vp, _vp]),
+    "block_pool_step": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, ctypes.c_int64, ctypes.c_int32,
+                                       _vp, _vp, _vp, ctypes.c_int32, _vp, _vp]),
     "paged_attn_error_string": (ctypes.c_char_p, []),
     "paged_attn_version": (ctypes.c_char_p, []),
 }

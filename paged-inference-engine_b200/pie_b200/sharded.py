@@ -261,15 +261,15 @@ class KVHeadShardedDecoder:
 # long-context benchmark (strong scaling over KV heads)
 # ----------------------------------------------------------------------------
 def build_rank_pool(ctx: list[int], Hkv_local: int, D: int, BS: int, seed: int, device, outliers: float = 0.01):
-    """Seeded INT8 pool (per-token fp16 scales) for this rank's KV heads, built on the device."""
-    from .workloads import block_tables, quantize_rows_torch
+    """Seeded INT8 pool (per-token fp16 scales, head-major) for this rank's KV heads, built on the device."""
+    from .workloads import block_tables, empty_head_major_scales, quantize_rows_torch
 
     gen = torch.Generator().manual_seed(seed)
     bt, nblk, NB = block_tables(gen, ctx, BS)
     K = torch.empty(NB, BS, Hkv_local, D, dtype=torch.int8, device=device)
     V = torch.empty_like(K)
-    ks = torch.empty(NB, BS, Hkv_local, dtype=torch.float16, device=device)
-    vs = torch.empty_like(ks)
+    ks = empty_head_major_scales(NB, BS, Hkv_local, device=device)
+    vs = empty_head_major_scales(NB, BS, Hkv_local, device=device)
     dg = torch.Generator(device=device).manual_seed(seed)
     step = 16384
     for lo in range(0, NB, step):

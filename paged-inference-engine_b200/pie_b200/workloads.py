@@ -102,12 +102,28 @@ def make_decode_batch(seed: int, B: int, Hq: int, Hkv: int, D: int, BS: int, ctx
         V16 = _normal(gen, (NB, BS, Hkv, D), torch.float16, outliers)
         K, ks = quantize_rows_torch(K16, scale_dtype)
         V, vs = quantize_rows_torch(V16, scale_dtype)
+        ks, vs = head_major(ks), head_major(vs)
     else:
         K = _normal(gen, (NB, BS, Hkv, D), kv_dtype, outliers)
         V = _normal(gen, (NB, BS, Hkv, D), kv_dtype, outliers)
         ks = vs = None
     return PagedBatch(Q, K, V, ks, vs, bt, nblk, torch.full((B,), q_len, dtype=torch.int32),
                       torch.tensor(ctx, dtype=torch.int32), BS)
+
+
+def head_major(scales: torch.Tensor) -> torch.Tensor:
+    """Per-token scales [NB, BS, H] stored head-major ([NB, H, BS] in memory), as the same [NB, BS, H] view.
+
+    The attention kernels read a tile's scales one KV head at a time: in this
+    layout the 16 scales of one head and block are one 32-byte sector, where
+    the slot-major layout spreads them over 16 * H * 2 bytes.
+    """
+    return scales.transpose(1, 2).contiguous().transpose(1, 2)
+
+
+def empty_head_major_scales(NB: int, BS: int, H: int, dtype=torch.float16, device=None) -> torch.Tensor:
+    """Uninitialised per-token scales [NB, BS, H] in the head-major layout of ``head_major``."""
+    return torch.empty(NB, H, BS, dtype=dtype, device=device).transpose(1, 2)
 
 
 def quantize_rows_torch(x: torch.Tensor, scale_dtype=torch.float16) -> tuple[torch.Tensor, torch.Tensor]:

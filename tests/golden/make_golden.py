@@ -398,6 +398,84 @@ def case_model_layer():
     np.savez_compressed(os.path.join(OUT, "model_layer_steps.npz"), **out)
 
 
+def case_block_trace():
+    """The reference's own Scheduler + BlockManager over a seeded request trace.
+
+    Records every allocate / release call (with its status), and after each
+    scheduling step the free list, the per-sequence block lists, the step's
+    metadata (core/model_runner.py:66-107) and the padded block table
+    (transformer/model.py:126-152).  A small pool makes INSUFFICIENT_SPACE,
+    skipped admissions and the scheduler's blocking mode occur.
+    """
+    from core.block_manager import BlockManager
+    from core.scheduler import Scheduler
+    from core.sequence import Sequence
+
+    sys.path.insert(0, os.path.dirname(OUT))
+    from oracle import block_manager as obm
+
+    NB, BS, MAXLEN, STEPS = 48, 16, 100, 70
+    bm = BlockManager(NB, BS)
+    ops = []  # (step, kind 0 = allocate / 1 = release, seq_id, n, status)
+    cur = [0]
+    alloc0, rel0 = bm.allocate, bm.release_blocks
+
+    def alloc(seq_id, n):
+        r = alloc0(seq_id, n)
+        ops.append((cur[0], 0, seq_id, n, r.status.value))
+        return r
+
+    def rel(seq_id):
+        r = rel0(seq_id)
+        ops.append((cur[0], 1, seq_id, 0, r.value))
+        return r
+
+    bm.allocate, bm.release_blocks = alloc, rel
+    sched = Scheduler(bm, BS, MAXLEN, skip_threshold=3, lookahead=5)
+    gen = torch.Generator().manual_seed(31)
+    rnd = lambda lo, hi: int(torch.randint(lo, hi + 1, (1,), generator=gen))  # noqa: E731
+    out = {}
+    next_id = 0
+    for step in range(STEPS):
+        cur[0] = step
+        if step < 45:
+            for _ in range(rnd(0, 2)):
+                sched.add_request(Sequence(seq_id=next_id, prompt_token_ids=[rnd(0, 999) for _ in range(rnd(5, 90))]))
+                next_id += 1
+        if step == 30:
+            bm.release_blocks(10 ** 6)  # an unknown sequence: FAILURE (core/block_manager.py:49-50)
+        so = sched.schedule()
+        pre = [(s.seq_id, len(s.prompt_token_ids), len(s.token_ids)) for s in so.prefill_seqs]
+        dec = [(s.seq_id, len(s.prompt_token_ids), len(s.token_ids)) for s in so.decode_seqs]
+        md = obm.step_metadata(pre, dec)
+        rows, nblk = obm.padded_block_table(bm.block_table, md["sequence_id"])
+        W = max(nblk) if nblk else 0
+        out[f"s{step}_stack"] = np.asarray(bm.st, np.int32)
+        seqs = sorted(bm.block_table)
+        out[f"s{step}_table_seq"] = np.asarray(seqs, np.int32)
+        out[f"s{step}_table_len"] = np.asarray([len(bm.block_table[q]) for q in seqs], np.int32)
+        out[f"s{step}_table_ids"] = np.asarray([b for q in seqs for b in bm.block_table[q]], np.int32)
+        out[f"s{step}_seq_info"] = np.asarray([(sid, npr, ntk, 1) for sid, npr, ntk in pre] +
+                                              [(sid, npr, ntk, 0) for sid, npr, ntk in dec], np.int32).reshape(-1, 4)
+        for k, v in md.items():
+            out[f"s{step}_{k}"] = np.asarray(v, np.int32)
+        out[f"s{step}_block_table"] = np.asarray(rows, np.int32).reshape(len(rows), W)
+        out[f"s{step}_num_blocks"] = np.asarray(nblk, np.int32)
+        for s_ in so.prefill_seqs + so.decode_seqs:  # one new token; some sequences end (EOS)
+            if rnd(0, 99) < 7:
+                s_.is_finished = True
+            else:
+                s_.token_ids.append(rnd(0, 999))
+    out["ops"] = np.asarray(ops, np.int32)
+    out["steps"] = np.int32(STEPS)
+    out["num_blocks"] = np.int32(NB)
+    out["block_size"] = np.int32(BS)
+    st = out["ops"][:, 4]
+    print(f"block_trace: {len(ops)} ops, {int((st == 1).sum())} insufficient, {int((st == 2).sum())} failure, "
+          f"{next_id} sequences")
+    np.savez_compressed(os.path.join(OUT, "block_trace.npz"), **out)
+
+
 CASES = {
     "quant": case_quant,
     "reference_test": case_reference_test,
@@ -412,6 +490,7 @@ CASES = {
     "gqa_int8_chunked_bs32": lambda: case_gqa("gqa_int8_chunked_bs32", 4, 1, 128, 32, [65, 90], [7, 33], True, 14),
     "top_left": case_top_left,
     "model_layer": case_model_layer,
+    "block_trace": case_block_trace,
 }
 
 if __name__ == "__main__":

@@ -38,9 +38,10 @@ def test_library_exports_every_header_function():
 
 def test_struct_layouts_match_header(tmp_path):
     from pie_b200 import _lib
+    from pie_b200.block_pool import PaBlockPool
 
     structs = {"pa_kv_cache_t": _lib.PaKvCache, "pa_paging_t": _lib.PaPaging, "pa_attn_io_t": _lib.PaAttnIO,
-               "pa_kv_new_t": _lib.PaKvNew}
+               "pa_kv_new_t": _lib.PaKvNew, "pa_block_pool_t": PaBlockPool}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "paged_attn_b200.h"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
@@ -209,3 +210,25 @@ def test_sharded_decoder_exchange_option():
     # a single process takes the local path: no exchange, no GPU
     out = dec.forward(torch.zeros(1, 8, 1, 64), None, None, None, None, None, 16, None)
     assert out.shape == (1, 8, 1, 64)
+
+
+def test_block_pool_argument_validation():
+    """block_pool_* reject bad descriptors on the host (no launch, no GPU needed)."""
+    from pie_b200 import _lib
+    from pie_b200.block_pool import PaBlockPool
+
+    lib = _lib.load()
+    assert lib.block_pool_init(None, None) == _lib.PA_ERR_INVALID
+    d = PaBlockPool(1 << 20, 1 << 20, 1 << 20, 1 << 20, 4, 16, 8, 8, 0)  # table_stride 4 < 8 columns
+    assert lib.block_pool_init(ctypes.byref(d), None) == _lib.PA_ERR_INVALID
+    assert b"table_stride" in lib.paged_attn_error_string()
+    d = PaBlockPool(None, 1 << 20, 1 << 20, 1 << 20, 8, 16, 8, 8, 0)
+    assert lib.block_pool_apply(ctypes.byref(d), 1 << 20, 1, None, None) == _lib.PA_ERR_INVALID
+    d = PaBlockPool(1 << 20, 1 << 20, 1 << 20, 1 << 20, 8, 16, 8, 8, 0)
+    assert lib.block_pool_apply(ctypes.byref(d), None, 3, None, None) == _lib.PA_ERR_INVALID
+    assert lib.block_pool_apply(ctypes.byref(d), None, -1, None, None) == _lib.PA_ERR_INVALID
+    assert lib.block_pool_apply(ctypes.byref(d), None, 0, None, None) == _lib.PA_OK  # nothing to do
+    assert lib.block_pool_step(ctypes.byref(d), None, None, None, None, 2, None, 4, 4, None, None, None, 2, None,
+                               None) == _lib.PA_ERR_INVALID
+    assert lib.block_pool_step(ctypes.byref(d), None, None, None, None, 0, None, 0, 0, None, None, None, 0, None,
+                               None) == _lib.PA_OK
