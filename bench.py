@@ -387,6 +387,7 @@ class PrefillWorkload(Workload):
         Hkv, D = self.kn.shape[1], self.kn.shape[2]
         Kc = torch.empty(self.NB, self.BS, Hkv, D, dtype=torch.float16, device=device)
         Vc = torch.empty_like(Kc)
+        self.dev = dict(Q=Qd, K=Kc, V=Vc, bt=btd, nb=nbd, L=Ld, kn=knd, vn=vnd, seq=seqd, pos=posd)
 
         def attend(out=None):
             return flash_attention_forward(Qd, Kc, Vc, Ld, btd, nbd, self.BS, Ld, None, None, out=out)
@@ -643,6 +644,84 @@ def measure(w: Workload, a, device, ws: int, rank: int, local: int, peaks: dict,
 
 
 EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16")
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def load_reference_kernel_module():
+    """The reference's unmodified kernels/flash_attention.py from baseline/_ref, under its own module name."""
+    import importlib.util
+
+    path = os.path.join(REF_DIR, "kernels", "flash_attention.py")
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} missing (python baseline/install_reference.py REFERENCE_ROOT)")
+    spec = importlib.util.spec_from_file_location("reference_flash_attention", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_kernel_leg(w: Workload, a, device) -> dict:
+    """The reference's own GPU kernel on this workload, through its own launcher, on this B200.
+
+    ``flash_attention_forward`` (kernels/flash_attention.py:139-172, Triton JIT
+    for sm_100, first call autotunes) with the inputs the reference's kernel
+    accepts: float32 Q (its tl.dot needs float32 operands), K/V heads expanded
+    to the query heads (it has no grouped-query attention), unit float32
+    per-(block, head) scales for float16 pools, per-block scales for INT8
+    pools (its only scale layout).  Decode calls use q_len = 1: the kernel's
+    top-left mask then lets the query see key 0 only (its output is not a
+    decode result), but every program still loads and multiplies every block
+    of its sequence, so the time is that of its decode.  Prefill calls are
+    exact (q_len = kv_len).  Reported against the workload's own algorithmic
+    work: the same bytes or causal FLOPs as ``value``.
+    """
+    try:
+        import triton
+
+        ref = load_reference_kernel_module()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    try:
+        if w.name == "prefill_bf16":
+            d = w.dev
+            from kernels.flash_attention import write_kv_cache
+
+            write_kv_cache(d["kn"], d["vn"], d["bt"], d["seq"], d["pos"], d["K"], d["V"])
+            G = d["Q"].shape[1] // d["K"].shape[2]
+            Q = d["Q"].float()
+            Kx = d["K"].repeat_interleave(G, dim=2)
+            Vx = d["V"].repeat_interleave(G, dim=2)
+            ones = torch.ones(Kx.shape[0], Kx.shape[2], dtype=torch.float32, device=device)
+            args = (Q, Kx, Vx, d["L"], d["bt"], d["nb"], w.BS, d["L"], ones, ones)
+            note = "prefill rows (q_len = kv_len), K/V heads expanded x4, float32 Q"
+        else:
+            g = w.g
+            G = g.Q.shape[1] // g.K.shape[2]
+            Q = g.Q.float()
+            Kx = g.K.repeat_interleave(G, dim=2)
+            Vx = g.V.repeat_interleave(G, dim=2)
+            if g.K.dtype == torch.int8:
+                ks = g.k_scale.float().amax(dim=1).repeat_interleave(G, dim=1).contiguous()
+                vs = g.v_scale.float().amax(dim=1).repeat_interleave(G, dim=1).contiguous()
+                note = "q_len 1 (top-left mask), INT8 pool with per-(block, head) scales, heads expanded x4"
+            else:
+                ks = vs = torch.ones(Kx.shape[0], Kx.shape[2], dtype=torch.float32, device=device)
+                note = "q_len 1 (top-left mask), fp16 pool, heads expanded x4"
+            args = (Q, Kx, Vx, g.q_len, g.block_table, g.num_blocks, g.block_size, g.kv_len, ks, vs)
+        t0 = time.perf_counter()
+        ref.flash_attention_forward(*args)  # compiles and autotunes
+        torch.cuda.synchronize(device)
+        first_s = time.perf_counter() - t0
+        ms = time_steps(lambda: ref.flash_attention_forward(*args), a.steps, a.warmup, device, 1) / a.steps
+        val = w.dominant_work / (ms * 1e-3) * w.scale
+        best = getattr(ref.flash_attention_kernel, "best_config", None)
+        return {"impl": "reference Triton kernel, unmodified (baseline/_ref/kernels/flash_attention.py)",
+                "triton": triton.__version__, "value": round(val, 3), "unit": w.unit,
+                "us_per_call": round(ms * 1e3, 2), "first_call_s": round(first_s, 2),
+                "best_config": str(best) if best is not None else None, "inputs": note,
+                "ours_over_reference": None}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
 
 
 def main():
@@ -659,6 +738,8 @@ def main():
                     help="one GPU: skip the records of the other workloads under the 'workloads' key")
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
                     help="long_ctx_int8 head-output exchange: NCCL all-gather or stores into peer buffers")
+    ap.add_argument("--no-reference-kernel", action="store_true",
+                    help="one GPU: skip timing the reference's own Triton kernel on the extra workloads")
     ap.add_argument("--batch", type=int, default=0,
                     help="long_ctx_int8 with fewer sequences (same context-length draws), for small profiler "
                          "captures; 0 = the workload's 256")
@@ -692,8 +773,13 @@ def main():
             if name == a.workload:
                 continue
             wx = make_workload(name, ws, rank, device)
-            line["workloads"][name] = measure(wx, a, device, ws, rank, local, peaks, peak_kind,
-                                              not a.no_cpu_baseline)
+            rx = measure(wx, a, device, ws, rank, local, peaks, peak_kind, not a.no_cpu_baseline)
+            if not a.no_reference_kernel:
+                rk = reference_kernel_leg(wx, a, device)
+                if "value" in rk:
+                    rk["ours_over_reference"] = round(rx["roofline"]["achieved"] / rk["value"], 2)
+                rx["reference_gpu_kernel"] = rk
+            line["workloads"][name] = rx
             del wx
             torch.cuda.empty_cache()
     if ws > 1:
