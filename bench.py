@@ -627,7 +627,7 @@ def measure(w: Workload, a, device, ws: int, rank: int, local: int, peaks: dict,
                                    else f"dp{ws} (one batch per rank)"),
                    "l2": "inputs larger than L2 (126 MB)"},
         "roofline": {"bound": w.bound, "achieved": round(dom, 2), "peak": peak, "unit": punit,
-                     "frac": round(dom / peak, 4), "traffic": read_traffic(f"{w.name}_dominant_kernel"),
+                     "frac": round(dom / peak, 4), "traffic": rank_traffic(w, ws),
                      "kernel": w.dominant_name, "us_per_launch": round(dom_ms * 1e3, 2),
                      "step_achieved": round(per_gpu, 2), "step_frac": round(per_gpu / peak, 4),
                      "step_kernels": w.kernel, "peak_source": f"{peak_kind} MEASURED_PEAKS"},
@@ -722,6 +722,14 @@ def reference_kernel_leg(w: Workload, a, device) -> dict:
                 "ours_over_reference": None}
     except Exception as e:  # noqa: BLE001
         return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+def rank_traffic(w: Workload, ws: int):
+    """DRAM bytes of one dominant launch on one rank (a strong-scaled rank reads 1/ws of the pool)."""
+    t = read_traffic(f"{w.name}_dominant_kernel")
+    if t is None:
+        return None
+    return round(t / ws) if w.scaling == "strong" else t
 
 
 def main():
