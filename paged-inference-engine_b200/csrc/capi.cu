@@ -175,8 +175,10 @@ int build_attn(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_
 
 // The split-K decode kernels read 16-bit and int8 pools; fp32 pools (a
 // reference-compatible format, not a serving one) always take the tiled kernel.
+// Batches of more than kMaxDecodeSeqs sequences decode in launches of at most
+// that many (run_decode).
 bool use_decode(const pa::AttnParams& p, const pa_kv_cache_t* kv) {
-  return p.maxq * p.G <= kNcMax && p.B <= kMaxDecodeSeqs && kv->dtype != PA_DTYPE_F32;
+  return p.maxq * p.G <= kNcMax && kv->dtype != PA_DTYPE_F32;
 }
 int decode_nt(const pa::AttnParams& p) { return p.maxq * p.G <= 8 ? 1 : 2; }
 int kv_kind(int dtype) {
@@ -270,10 +272,53 @@ WsLayout ws_layout(int warps, int D, int B) {
   return l;
 }
 
+int run_decode_launch(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream,
+                      int phase, int plan_B);
+
+// The sequences [first, first + n) of a decode problem as a problem of their
+// own: every per-sequence pointer moves to row `first` (ragged rows keep their
+// absolute row offsets through q_start).
+pa::AttnParams seq_slice(const pa::AttnParams& p, int first, int n) {
+  pa::AttnParams c = p;
+  const long long f = first;
+  c.bt = p.bt + f * p.bt_ss;
+  c.nblk = p.nblk + f;
+  c.qlen = p.qlen + f;
+  c.kvlen = p.kvlen + f;
+  if (p.q_start) {
+    c.q_start = p.q_start + f;
+  } else {
+    c.q = static_cast<const unsigned short*>(p.q) + f * p.q_sb;
+    c.o = static_cast<uint16_t*>(p.o) + f * p.o_sb;
+    for (int r = 0; r < p.n_peers; ++r) c.o_peer[r] = static_cast<uint16_t*>(p.o_peer[r]) + f * p.o_sb;
+    if (p.lse) c.lse = static_cast<uint16_t*>(p.lse) + f * p.l_sb;
+  }
+  c.B = n;
+  return c;
+}
+
+// Split-K decode of any number of sequences: launches of at most
+// kMaxDecodeSeqs sequences (the per-sequence tile scan of one launch lives in
+// shared memory), one after another on the stream, sharing the workspace.
+// Every launch of a split batch uses the launch plan of a full one, so the
+// workspace that paged_attn_workspace_size reports fits each of them.
 int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream,
                int phase = pa::DECODE_BOTH) {
+  if (p.B <= kMaxDecodeSeqs) return run_decode_launch(p, kv, ws, ws_bytes, stream, phase, p.B);
+  if (phase != pa::DECODE_BOTH)
+    return fail(PA_ERR_UNSUPPORTED, "split / reduce as separate calls take at most %d sequences", kMaxDecodeSeqs);
+  for (int first = 0; first < p.B; first += kMaxDecodeSeqs) {
+    pa::AttnParams c = seq_slice(p, first, p.B - first < kMaxDecodeSeqs ? p.B - first : kMaxDecodeSeqs);
+    const int rc = run_decode_launch(c, kv, ws, ws_bytes, stream, phase, kMaxDecodeSeqs);
+    if (rc) return rc;
+  }
+  return PA_OK;
+}
+
+int run_decode_launch(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_bytes, void* stream,
+                      int phase, int plan_B) {
   if (p.B > kMaxDecodeSeqs)
-    return fail(PA_ERR_UNSUPPORTED, "decode kernel supports at most %d sequences per call", kMaxDecodeSeqs);
+    return fail(PA_ERR_UNSUPPORTED, "decode kernel supports at most %d sequences per launch", kMaxDecodeSeqs);
   if (p.maxq * p.G > kNcMax)
     return fail(PA_ERR_UNSUPPORTED, "decode kernel packs at most %d (q rows x group heads) columns", kNcMax);
   if (kv->dtype == PA_DTYPE_F32)
@@ -284,10 +329,10 @@ int run_decode(pa::AttnParams& p, const pa_kv_cache_t* kv, void* ws, size_t ws_b
   pa::KvMaps maps;
   const bool tma = make_kv_maps(kv, &maps);
   pa::DecodeLaunch plan;
-  if (cached_plan(kv_k, p.q_bf16, kv->head_dim, nt, p.B, tma, &plan) != 0)
+  if (cached_plan(kv_k, p.q_bf16, kv->head_dim, nt, plan_B, tma, &plan) != 0)
     return fail(PA_ERR_CUDA, "could not plan the decode launch (no CUDA device?)");
   const int warps = plan.ctas * plan.warps_per_cta;
-  const WsLayout L = ws_layout(warps, kv->head_dim, p.B);
+  const WsLayout L = ws_layout(warps, kv->head_dim, plan_B);
   if (!ws || ws_bytes < L.total)
     return fail(PA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", L.total, ws_bytes);
   if (!al(ws, 256)) return fail(PA_ERR_WORKSPACE, "workspace must be 256-byte aligned");
@@ -454,12 +499,13 @@ int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   int rc = build_attn(io, kv, pg, nullptr, p);
   if (rc) return rc;
   if (!use_decode(p, kv) || p.B == 0 || p.maxq == 0) return PA_OK;
+  const int per_launch = p.B < kMaxDecodeSeqs ? p.B : kMaxDecodeSeqs;
   pa::KvMaps maps;
   const bool tma = make_kv_maps(kv, &maps);
   pa::DecodeLaunch plan;
-  if (cached_plan(kv_kind(kv->dtype), p.q_bf16, kv->head_dim, decode_nt(p), p.B, tma, &plan) != 0)
+  if (cached_plan(kv_kind(kv->dtype), p.q_bf16, kv->head_dim, decode_nt(p), per_launch, tma, &plan) != 0)
     return fail(PA_ERR_CUDA, "could not plan the decode launch (no CUDA device?)");
-  *bytes = ws_layout(plan.ctas * plan.warps_per_cta, kv->head_dim, p.B).total;
+  *bytes = ws_layout(plan.ctas * plan.warps_per_cta, kv->head_dim, per_launch).total;
   return PA_OK;
 }
 

@@ -1,11 +1,15 @@
-"""KV-head sharded paged decode across the GPUs of one node.
+"""KV-head sharded paged attention (decode and prefill) across the GPUs of one node.
 
 Attention has no cross-head dependency, so rank r of a world of G ranks owns
 KV heads [r*Hkv/G, (r+1)*Hkv/G) -- its own block pool [NB_r, BS, Hkv/G, D]
 (and scales) -- and the Hq/G query heads that read them.  Each rank runs the
-split-K decode kernel on its local heads; one NCCL ``all_gather_into_tensor``
-over NVLink then assembles O for all heads in head order, which is only needed
-where the consumer wants every head (e.g. the output projection).
+attention kernels on its local heads (split-K decode for short query blocks,
+the tcgen05 prefill kernel for long ones: any query length); one NCCL
+``all_gather_into_tensor`` over NVLink then assembles O for all heads in head
+order, which is only needed where the consumer wants every head (e.g. the
+output projection).  Sharding by sequence needs no collective at all: every
+rank runs its own sequences with all heads (the replicas of bench.py's
+per-rank batches).
 
 The reference has no multi-GPU path; this module is the B200 scaling layer for
 the paged-attention hot path (kernels/flash_attention.py:139-172 per rank).
@@ -164,15 +168,19 @@ class PeerOutputExchange:
 
 
 class KVHeadShardedDecoder:
-    """Per-rank decode over the local KV heads + all-gather of head outputs.
+    """Per-rank attention over the local KV heads + all-gather of head outputs.
+
+    Works for any query length (decode, prefill, chunked prefill): the local
+    call dispatches like ``flash_attention_forward``.
 
     ``attention_fn(Q_local, K, V, q_len, block_table, num_blocks, block_size,
     kv_len, k_scale, v_scale) -> (O, L)`` computes the local heads; it defaults
     to the CUDA ``flash_attention_forward``.  The gather uses the default
     process group (NCCL on GPUs; any backend works for the host logic).
 
-    ``exchange="peer"`` (GPUs of one box, decode shapes) replaces the
-    all-gather by the fused exchange: the decode kernels store every finished
+    ``exchange="peer"`` (GPUs of one box) replaces the all-gather by the
+    fused exchange for decode shapes (max_q_len * Hq / Hkv <= 16; longer
+    query blocks use the all-gather): the decode kernels store every finished
     output row into every rank's mapped output buffer and a cross-GPU flag
     barrier ends the step.  The returned tensor is then one of two buffers the
     steps alternate between: consume it on the current stream before the
@@ -223,8 +231,9 @@ class KVHeadShardedDecoder:
 
     def forward(self, Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale=None,
                 v_scale=None, gather: bool = True):
-        """Returns O for all heads [B, Hq, q, D] (gather=True) or the local heads."""
-        if gather and self.world > 1 and self.exchange == "peer":
+        """Returns O for all heads [B, Hq, q, D] (gather=True) or the local heads [B, Hq/G, q, D]."""
+        decode_shape = Q_local.shape[2] * (self.Hq // self.Hkv) <= 16
+        if gather and self.world > 1 and self.exchange == "peer" and decode_shape:
             return self._forward_peer(Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale,
                                       v_scale)
         O_loc, _ = self.attention_fn(Q_local, K, V, q_len, block_table, num_blocks, block_size, kv_len, k_scale,
@@ -255,6 +264,9 @@ class KVHeadShardedDecoder:
             self._gather_buf = torch.empty(n * self.world, dtype=O_loc.dtype, device=O_loc.device)
         dist.all_gather_into_tensor(self._gather_buf, O_loc.contiguous().view(-1), group=self.group)
         return self._gather_buf.view(self.world, B, hl, q, D).permute(1, 0, 2, 3, 4).reshape(B, self.world * hl, q, D)
+
+
+KVHeadShardedAttention = KVHeadShardedDecoder  # the same layer, named for any query length
 
 
 # ----------------------------------------------------------------------------

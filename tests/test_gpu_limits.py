@@ -1,7 +1,8 @@
 """Parity at the size limits of the kernels.
 
-* 8192 sequences, the most one decode launch takes, and 8193, which
-  flash_attention_forward serves with the prefill kernel instead;
+* 8192 sequences, the most one decode launch takes, and 8193 and 20000,
+  which the decode path serves in launches of at most 8192 sequences that
+  share one workspace;
 * the decode / prefill switch at exactly 16 packed columns
   (max_q_len * Hq / Hkv = 16 decodes, 20 does not);
 * one sequence of 131072 keys (8192 blocks of 16).
@@ -37,19 +38,29 @@ def _check(b, O, L, rows, q_len, tol=TOL_F16):
         np.testing.assert_allclose(L[bi, :, :n].float().cpu().numpy(), L_or[i, :, :n], atol=1e-2, rtol=1e-3)
 
 
-@pytest.mark.parametrize("B", [8192, 8193])
-def test_most_sequences_per_launch(B):
+@pytest.mark.parametrize("B,kv_dtype", [(8192, torch.float16), (8193, torch.float16), (20000, torch.float16),
+                                         (8200, torch.int8)])
+def test_most_sequences_per_launch(B, kv_dtype):
     from kernels.flash_attention import flash_attention_forward
+    from pie_b200 import ops
     from pie_b200.workloads import make_decode_batch
 
     gen = np.random.default_rng(B)
     ctx = [int(c) for c in gen.integers(1, 48, size=B)]
-    b = make_decode_batch(B, B, 8, 2, 128, 16, ctx)
+    b = make_decode_batch(B, B, 8, 2, 128, 16, ctx, kv_dtype=kv_dtype)
     g = b.to("cuda")
-    O, L = flash_attention_forward(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, 16, g.kv_len)
+    O, L = flash_attention_forward(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, 16, g.kv_len, g.k_scale,
+                                   g.v_scale)
     torch.cuda.synchronize()
-    rows = sorted(set([0, 1, B // 2, B - 2, B - 1] + [int(x) for x in gen.integers(0, B, size=120)]))
-    _check(b, O, L, rows, b.q_len.numpy())
+    rows = sorted(set([0, 1, 8191, 8192, B // 2, B - 2, B - 1] + [int(x) for x in gen.integers(0, B, size=120)]))
+    rows = [r for r in rows if r < B]
+    tol = 2e-2 if kv_dtype == torch.int8 else TOL_F16
+    _check(b, O, L, rows, b.q_len.numpy(), tol=tol)
+    # the decode entry point itself takes the whole batch (no switch to the prefill kernel)
+    O2, L2 = ops.paged_attention(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, 16, g.kv_len, g.k_scale,
+                                 g.v_scale, mode="decode")
+    torch.cuda.synchronize()
+    assert torch.equal(O, O2) and torch.equal(L, L2)
 
 
 @pytest.mark.parametrize("qmax", [4, 5])

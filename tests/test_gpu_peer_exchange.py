@@ -60,6 +60,48 @@ def _rank(rank, world, port):
         dist.destroy_process_group()
 
 
+def _rank_prefill(rank, world, port):
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "paged-inference-engine_b200"))
+    import torch.distributed as dist
+    from kernels.flash_attention import flash_attention_forward
+    from pie_b200.sharded import KVHeadShardedAttention
+    from pie_b200.workloads import make_decode_batch
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        Hq, Hkv, D = 16, 4, 128
+        ctx = [700, 1300, 257]
+        b = make_decode_batch(31, len(ctx), Hq, Hkv, D, 16, ctx, q_len=300)  # the same batch on every rank
+        b.q_len = torch.tensor([300, 300, 257], dtype=torch.int32)
+        g = b.to(dev)
+        sh = KVHeadShardedAttention(Hq, Hkv, D)
+        lo, hi = sh.kv_lo, sh.kv_hi
+        K, V = g.K[:, :, lo:hi].contiguous(), g.V[:, :, lo:hi].contiguous()
+        got = sh.forward(sh.local_q(g.Q).contiguous(), K, V, g.q_len, g.block_table, g.num_blocks, 16, g.kv_len)
+        want, _ = flash_attention_forward(g.Q, g.K, g.V, g.q_len, g.block_table, g.num_blocks, 16, g.kv_len)
+        torch.cuda.synchronize()
+        for i, n in enumerate(b.q_len.tolist()):
+            assert torch.equal(got[i, :, :n], want[i, :, :n]), f"rank {rank} sequence {i}"
+        dist.barrier()
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one box")
+def test_kv_head_sharded_prefill_matches_one_gpu():
+    """Prefill sharded over two GPUs by KV head equals the one-GPU call bit for bit."""
+    mp.spawn(_rank_prefill, args=(2, _free_port()), nprocs=2, join=True)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs of one box")
 def test_peer_exchange_matches_all_gather():
     mp.spawn(_rank, args=(2, _free_port()), nprocs=2, join=True)

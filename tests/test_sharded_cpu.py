@@ -33,7 +33,7 @@ def _oracle_attention(Q, K, V, q_len, bt, nblk, bs, kv_len, ks, vs):
     return torch.from_numpy(O).half(), torch.from_numpy(L).half()
 
 
-def _worker(rank, world, port, result_path, fail_rank):
+def _worker(rank, world, port, result_path, fail_rank, q_len=1):
     import sys
 
     for p in (ROOT, PKG):
@@ -46,7 +46,9 @@ def _worker(rank, world, port, result_path, fail_rank):
     from pie_b200.workloads import make_decode_batch
 
     Hq, Hkv, D = 8, 4, 64
-    b = make_decode_batch(4, 3, Hq, Hkv, D, 16, [40, 17, 100], kv_dtype=torch.int8)  # same full batch everywhere
+    # same full batch everywhere; q_len > 1: prefill / chunked-prefill rows
+    b = make_decode_batch(4, 3, Hq, Hkv, D, 16, [40, 17, 100], kv_dtype=torch.int8, q_len=q_len)
+    b.q_len = torch.tensor([min(q_len, c) for c in (40, 17, 100)], dtype=torch.int32)
     dec = KVHeadShardedDecoder(Hq, Hkv, D, attention_fn=_oracle_attention)
     lo, hi = dec.kv_lo, dec.kv_hi
     K, V = b.K[:, :, lo:hi].contiguous(), b.V[:, :, lo:hi].contiguous()
@@ -70,11 +72,11 @@ def _worker(rank, world, port, result_path, fail_rank):
         pass
 
 
-def _run(world, fail_rank, tmp_path):
+def _run(world, fail_rank, tmp_path, q_len=1):
     ctx = mp.get_context("spawn")
     port = _free_port()
     out = str(tmp_path / "res")
-    procs = [ctx.Process(target=_worker, args=(r, world, port, out, fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, out, fail_rank, q_len)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -93,6 +95,12 @@ def test_head_range_split():
 
 def test_kv_head_sharded_gather_matches_full(tmp_path):
     res = _run(2, -1, tmp_path)
+    assert res == ["ok", "ok"], res
+
+
+def test_kv_head_sharded_prefill_matches_full(tmp_path):
+    """Prefill rows (q_len up to 33, bottom-right causal) through the same sharded layer."""
+    res = _run(2, -1, tmp_path, q_len=33)
     assert res == ["ok", "ok"], res
 
 
