@@ -1,9 +1,15 @@
-"""Torch-tensor front end of the C ABI: descriptors, workspace, streams.
+"""Torch-tensor front end of the C ABI: argument checks, then the registered torch ops.
 
 All tensors live on one CUDA device; every launch goes to torch's current
 stream on that device, so calls compose with torch ops and CUDA graphs.
 Nothing here computes on the host and there is no fallback path: a missing
 library or a non-CUDA tensor raises.
+
+The calls go through the torch.library ops of the extension
+(``torch.ops.pie_b200.*``, csrc/torch_ops.cpp), which fill the C structs and
+call libpaged_attn_b200.so in C++.  ``PIE_B200_BACKEND=ctypes`` routes the
+same calls through the ctypes binding of the C ABI instead (``_lib``): the
+two paths launch the same kernels with the same arguments.
 """
 from __future__ import annotations
 
@@ -24,6 +30,16 @@ _TORCH2PA = {
 }
 
 _CHECK = os.environ.get("PIE_B200_CHECK", "0") not in ("", "0")
+BACKEND = os.environ.get("PIE_B200_BACKEND", "torch")
+if BACKEND not in ("torch", "ctypes"):
+    raise ValueError(f"PIE_B200_BACKEND must be 'torch' or 'ctypes', not {BACKEND!r}")
+_MODES = {"auto": 0, "decode": 1, "prefill": 2}
+
+
+def _torch_ops():
+    from . import _torch_ext
+
+    return _torch_ext.ops()
 
 
 def _i32(t: torch.Tensor) -> torch.Tensor:
@@ -43,15 +59,7 @@ def kv_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: Optiona
     Scales: [num_blocks, num_kv_heads] (one per block and head, the reference
     layout) or [num_blocks, block_size, num_kv_heads] (one per token and head).
     """
-    if k_cache.dim() != 4 or v_cache.dim() != 4:
-        raise ValueError("K/V pools must be 4-D [num_blocks, block_size, num_kv_heads, head_dim]")
-    if k_cache.shape != v_cache.shape or k_cache.dtype != v_cache.dtype:
-        raise ValueError(f"K and V pools differ: {tuple(k_cache.shape)}/{k_cache.dtype} vs "
-                         f"{tuple(v_cache.shape)}/{v_cache.dtype}")
-    if k_cache.dtype not in (torch.float16, torch.bfloat16, torch.int8, torch.float32):
-        raise ValueError(f"KV pool dtype {k_cache.dtype} unsupported (float16, bfloat16, int8 or float32)")
-    if k_cache.stride(3) != 1 or v_cache.stride(3) != 1:
-        raise ValueError("KV pools need a contiguous head_dim")
+    check_cache(k_cache, v_cache, k_scale, v_scale)
     nb, bs, h, d = k_cache.shape
     kc = PaKvCache()
     kc.k = k_cache.data_ptr()
@@ -62,6 +70,28 @@ def kv_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: Optiona
     kc.v_stride_block, kc.v_stride_slot, kc.v_stride_head = v_cache.stride(0), v_cache.stride(1), v_cache.stride(2)
     kc.scale_dtype = _lib.PA_DTYPE_F16
     if k_cache.dtype == torch.int8:
+        kc.scale_dtype = _TORCH2PA[k_scale.dtype]
+        kc.k_scale = k_scale.data_ptr()
+        kc.v_scale = v_scale.data_ptr()
+        kc.ks_stride_block, kc.ks_stride_slot, kc.ks_stride_head = _scale_strides(k_scale, nb, bs, h)
+        kc.vs_stride_block, kc.vs_stride_slot, kc.vs_stride_head = _scale_strides(v_scale, nb, bs, h)
+    return kc
+
+
+def check_cache(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: Optional[torch.Tensor] = None,
+                v_scale: Optional[torch.Tensor] = None) -> None:
+    """Raise ValueError unless the pools (and an INT8 pool's scales) are well formed."""
+    if k_cache.dim() != 4 or v_cache.dim() != 4:
+        raise ValueError("K/V pools must be 4-D [num_blocks, block_size, num_kv_heads, head_dim]")
+    if k_cache.shape != v_cache.shape or k_cache.dtype != v_cache.dtype:
+        raise ValueError(f"K and V pools differ: {tuple(k_cache.shape)}/{k_cache.dtype} vs "
+                         f"{tuple(v_cache.shape)}/{v_cache.dtype}")
+    if k_cache.dtype not in (torch.float16, torch.bfloat16, torch.int8, torch.float32):
+        raise ValueError(f"KV pool dtype {k_cache.dtype} unsupported (float16, bfloat16, int8 or float32)")
+    if k_cache.stride(3) != 1 or v_cache.stride(3) != 1:
+        raise ValueError("KV pools need a contiguous head_dim")
+    nb, bs, h, d = k_cache.shape
+    if k_cache.dtype == torch.int8:
         if k_scale is None or v_scale is None:
             raise ValueError("an int8 KV pool needs k_scale and v_scale")
         for name, s in (("k_scale", k_scale), ("v_scale", v_scale)):
@@ -71,12 +101,8 @@ def kv_cache_desc(k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: Optiona
                 raise ValueError(f"{name} is on {s.device}, the pool on {k_cache.device}")
         if k_scale.dtype != v_scale.dtype:
             raise ValueError("k_scale and v_scale dtypes differ")
-        kc.scale_dtype = _TORCH2PA[k_scale.dtype]
-        kc.k_scale = k_scale.data_ptr()
-        kc.v_scale = v_scale.data_ptr()
-        kc.ks_stride_block, kc.ks_stride_slot, kc.ks_stride_head = _scale_strides(k_scale, nb, bs, h)
-        kc.vs_stride_block, kc.vs_stride_slot, kc.vs_stride_head = _scale_strides(v_scale, nb, bs, h)
-    return kc
+        _scale_strides(k_scale, nb, bs, h)
+        _scale_strides(v_scale, nb, bs, h)
 
 
 def _scale_strides(s: torch.Tensor, nb: int, bs: int, h: int) -> tuple[int, int, int]:
@@ -105,6 +131,19 @@ def pool_layout(K: torch.Tensor, V: torch.Tensor, block_size: int) -> tuple[torc
     if K.dim() == 4 and K.shape[1] != block_size and K.shape[2] == block_size:
         return K.transpose(1, 2), V.transpose(1, 2)
     return K, V
+
+
+def _paging_tensors(block_table: torch.Tensor, num_blocks: torch.Tensor, q_len: torch.Tensor,
+                    kv_len: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """int32 block table (any strides) and contiguous int32 metadata with one entry per sequence."""
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    if bt.dim() != 2:
+        raise ValueError("block_table must be 2-D [num_seqs, max_blocks]")
+    nbk, ql, kl = _i32(num_blocks), _i32(q_len), _i32(kv_len)
+    for name, t in (("num_blocks_per_seq", nbk), ("q_len_per_seq", ql), ("kv_len_per_seq", kl)):
+        if t.numel() != bt.shape[0]:
+            raise ValueError(f"{name} has {t.numel()} entries for {bt.shape[0]} sequences")
+    return bt, nbk, ql, kl
 
 
 def paging_desc(block_table: torch.Tensor, num_blocks: torch.Tensor, q_len: torch.Tensor,
@@ -201,15 +240,28 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
         Q = Q.to(mma_dtype)
     if Q.stride(3) != 1:
         Q = Q.contiguous()
-    keep: list = []
-    kc = kv_cache_desc(K, V, k_scale, v_scale)
-    pg = paging_desc(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq, keep)
+    if mode not in _MODES:
+        raise ValueError(f"mode must be one of {sorted(_MODES)}, not {mode!r}")
     if out is None:
         out = torch.empty((B, Hq, maxq, D), dtype=torch.float16, device=dev)
     elif out.dtype != torch.float16 or tuple(out.shape) != (B, Hq, maxq, D):
         raise ValueError("out must be float16 with Q's shape")
     if lse is None:
         lse = torch.empty((B, Hq, maxq), dtype=torch.float16, device=dev)
+    if status is None and _CHECK:
+        status = status_word(dev)
+    if BACKEND == "torch":
+        check_cache(K, V, k_scale, v_scale)
+        bt, nbk, ql, kl = _paging_tensors(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq)
+        _torch_ops().paged_attention_out(Q, K, V, ql, bt, nbk, kl, k_scale, v_scale, bool(causal_top_left),
+                                         float(softmax_scale) if softmax_scale else 0.0, _MODES[mode], status, out,
+                                         lse)
+        if _CHECK and status is not None:
+            _raise_status("paged_attention", status)
+        return out, lse
+    keep: list = []
+    kc = kv_cache_desc(K, V, k_scale, v_scale)
+    pg = paging_desc(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq, keep)
     io = PaAttnIO()
     io.q = Q.data_ptr()
     io.q_dtype = _TORCH2PA[Q.dtype]
@@ -224,8 +276,6 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
 
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if status is None and _CHECK:
-        status = status_word(dev)
     st_ptr = _ptr(status)
     with torch.cuda.device(dev):
         if mode == "prefill":
@@ -281,15 +331,27 @@ def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch
         Q = Q.to(mma_dtype)
     if Q.stride(2) != 1:
         Q = Q.contiguous()
-    keep: list = [cu, q_len]
-    kc = kv_cache_desc(K, V, k_scale, v_scale)
-    pg = paging_desc(block_table, num_blocks_per_seq, q_len, kv_len_per_seq, keep)
     if out is None:
         out = torch.empty((T, Hq, D), dtype=torch.float16, device=dev)
     elif out.dtype != torch.float16 or tuple(out.shape) != (T, Hq, D):
         raise ValueError("out must be float16 with Q's shape")
     if lse is None:
         lse = torch.empty((T, Hq), dtype=torch.float16, device=dev)
+    if status is None and _CHECK:
+        status = status_word(dev)
+    if BACKEND == "torch":
+        check_cache(K, V, k_scale, v_scale)
+        bt, nbk, ql, kl = _paging_tensors(block_table, num_blocks_per_seq, q_len, kv_len_per_seq)
+        if T:
+            _torch_ops().paged_attention_varlen_out(Q, q_start, ql, int(max_q_len), K, V, bt, nbk, kl, k_scale,
+                                                    v_scale, bool(causal_top_left),
+                                                    float(softmax_scale) if softmax_scale else 0.0, status, out, lse)
+        if _CHECK and status is not None:
+            _raise_status("paged_attention_varlen", status)
+        return out, lse
+    keep: list = [cu, q_len]
+    kc = kv_cache_desc(K, V, k_scale, v_scale)
+    pg = paging_desc(block_table, num_blocks_per_seq, q_len, kv_len_per_seq, keep)
     io = PaAttnIO()
     io.q = Q.data_ptr()
     io.q_dtype = _TORCH2PA[Q.dtype]
@@ -304,8 +366,6 @@ def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch
 
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if status is None and _CHECK:
-        status = status_word(dev)
     st_ptr = _ptr(status)
     with torch.cuda.device(dev):
         nbytes = ctypes.c_size_t(0)
@@ -382,14 +442,26 @@ def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor
         k_new = k_new.contiguous()
     if v_new.stride(2) != 1:
         v_new = v_new.contiguous()
-    keep: list = []
-    kc = kv_cache_desc(k_cache, v_cache, k_scale, v_scale)
+    check_cache(k_cache, v_cache, k_scale, v_scale)
     if k_cache.dtype == torch.int8 and k_scale.dim() != 3:
         raise ValueError("quantise-on-write stores one scale per (token, head): scales must be [NB, BS, H]")
     bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
     si, ps = _i32(seq_index), _i32(positions)
     if si.numel() != T or ps.numel() != T:
         raise ValueError("seq_index / positions need one entry per token")
+    if status is None and _CHECK:
+        status = status_word(dev)
+    if BACKEND == "torch":
+        if bt.dim() != 2:
+            raise ValueError("block_table must be 2-D [num_seqs, max_blocks]")
+        _torch_ops().write_kv(k_new, v_new, bt, si, ps, k_cache, v_cache,
+                              k_scale if k_cache.dtype == torch.int8 else None,
+                              v_scale if k_cache.dtype == torch.int8 else None, status)
+        if _CHECK and status is not None:
+            _raise_status("write_kv_cache", status)
+        return
+    keep: list = []
+    kc = kv_cache_desc(k_cache, v_cache, k_scale, v_scale)
     keep.extend((bt, si, ps))
     pg = _lib.PaPaging()
     pg.block_table = bt.data_ptr()
@@ -404,8 +476,6 @@ def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor
     nw.seq_index, nw.positions = si.data_ptr(), ps.data_ptr()
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev).cuda_stream
-    if status is None and _CHECK:
-        status = status_word(dev)
     with torch.cuda.device(dev):
         if k_cache.dtype == torch.int8:
             _lib.check("kv_write_quant", lib.kv_write_quant(nw, kc, pg, _ptr(status), stream))

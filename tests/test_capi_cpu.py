@@ -232,3 +232,24 @@ def test_block_pool_argument_validation():
                                None) == _lib.PA_ERR_INVALID
     assert lib.block_pool_step(ctypes.byref(d), None, None, None, None, 0, None, 0, 0, None, None, None, 0, None,
                                None) == _lib.PA_OK
+
+
+def test_torch_extension_registers_the_ops():
+    """The torch.library extension loads without a GPU and its meta kernels give the output shapes."""
+    from pie_b200 import _torch_ext
+
+    ops = _torch_ext.ops()
+    for name in ("paged_attention", "paged_attention_out", "paged_attention_varlen", "paged_attention_varlen_out",
+                 "write_kv"):
+        assert hasattr(ops, name), name
+    meta = dict(device="meta")
+    Q = torch.empty(3, 8, 5, 128, dtype=torch.float16, **meta)
+    K = torch.empty(10, 16, 2, 128, dtype=torch.int8, **meta)
+    s = torch.empty(10, 16, 2, dtype=torch.float16, **meta)
+    i = torch.empty(3, dtype=torch.int32, **meta)
+    bt = torch.empty(3, 4, dtype=torch.int32, **meta)
+    O, L = ops.paged_attention(Q, K, K, i, bt, i, i, s, s, False, 0.0, 0, None)
+    assert O.shape == Q.shape and L.shape == (3, 8, 5) and O.dtype == torch.float16
+    q = torch.empty(11, 8, 128, dtype=torch.bfloat16, **meta)
+    O, L = ops.paged_attention_varlen(q, i, i, 5, K, K, bt, i, i, s, s, False, 0.0, None)
+    assert O.shape == q.shape and L.shape == (11, 8) and O.dtype == torch.float16
