@@ -57,6 +57,17 @@ constexpr int META_B = 16;      // per stage: [0] fp16 half-select mask of the s
 #ifndef PA_DEC_TILE_I8
 #define PA_DEC_TILE_I8 32
 #endif
+// INT8 pools: S = Q K^T on the integer MMA (PA_DEC_I8_IMMA = 1).  Each packed
+// Q column is quantised once per piece to 16-bit fixed point against its own
+// absmax (q ~ s_q * (256 * hi + lo), hi and lo int8) and the raw int8 K tile is
+// the A operand as it sits in shared memory: two m16n8k32 chains (hi, lo) give
+// sum_d k_d * v_d exactly in int32, so no K byte is converted.  Q keeps 15 bits
+// against its column maximum (an absolute error of amax / 65024 per element,
+// below fp16's 2^-11 relative for every element above amax / 32); the
+// reference dots a TF32-rounded Q.  0 keeps the fp16 path with biased operands.
+#ifndef PA_DEC_I8_IMMA
+#define PA_DEC_I8_IMMA 1
+#endif
 
 template <int D, int KVT>
 struct DecCfg {
@@ -312,6 +323,7 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   constexpr bool MMA_BF16 = (KVT == KV_BF16);
   constexpr bool QIS_BF16 = (QT == Q_BF16);
   constexpr bool USE_CPASYNC = !TMA || INT8;  // cp.async carries tiles (no TMA) or scale words (INT8)
+  constexpr bool IMMA = INT8 && PA_DEC_I8_IMMA;  // integer Q*K^T (see PA_DEC_I8_IMMA)
   constexpr int KS = D / 16;  // k-steps over head_dim / m-tiles of O^T
   constexpr int NC = 8 * NT;
 
@@ -452,8 +464,10 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
   int lim_min = 0;      // fewest visible keys over the warp's columns (warp-uniform)
   // INT8 (biased operands): I8_BIAS * sum_d q_d of this thread's S columns, and
   // the per-column sum of P' accumulated by an MMA with an all-ones A operand.
+  // With the integer Q*K^T (IMMA) qs holds the columns' fixed-point scales instead.
   float qs[NT][2];
   float acc1[NT][4];
+  float qscale_own[NT];  // IMMA: this thread's column (nt*8 + r) scale
   int piece_start_tile = 0;
   int qlen_b = 0;
   bool piece_first = true;  // first piece of this warp's range
@@ -498,6 +512,50 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
             qf[nt][kk][0] = cvt_pair<QIS_BF16, MMA_BF16>(w0);
             qf[nt][kk][1] = cvt_pair<QIS_BF16, MMA_BF16>(w1);
           }
+        } else if constexpr (IMMA) {
+          // this thread's 16 values of column nt*8 + r per 64 of head_dim (d = 64 gg + 16 q4 + 0..15)
+          float f[D / 64][16];
+          float amax = 0.f;
+#pragma unroll
+          for (int gg = 0; gg < D / 64; ++gg) {
+            uint4 a = make_uint4(0, 0, 0, 0), bq = make_uint4(0, 0, 0, 0);
+            if (valid) {
+              const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * gg + 16 * q4);
+              a = src[0];
+              bq = src[1];
+            }
+            const uint32_t w[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float2 v;
+              if constexpr (QIS_BF16) v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+              else v = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+              f[gg][2 * j] = v.x;
+              f[gg][2 * j + 1] = v.y;
+              amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
+            }
+          }
+          // the column's absmax over head_dim: the four threads of the row group
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+          const float inv = amax > 0.f ? 32512.f / amax : 0.f;
+          qscale_own[nt] = amax * (1.f / 32512.f);
+#pragma unroll
+          for (int gg = 0; gg < D / 64; ++gg)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint32_t hi = 0, lo = 0;
+#pragma unroll
+              for (int b8 = 0; b8 < 4; ++b8) {
+                const int v = __float2int_rn(f[gg][4 * j + b8] * inv);  // |v| <= 32512
+                const int h = (v + 128) >> 8;                             // [-127, 127]
+                const int l = v - (h << 8);                               // [-128, 127]
+                hi |= static_cast<uint32_t>(h & 0xff) << (8 * b8);
+                lo |= static_cast<uint32_t>(l & 0xff) << (8 * b8);
+              }
+              qf[nt][4 * gg + j][0] = hi;
+              qf[nt][4 * gg + j][1] = lo;
+            }
         } else {
 #pragma unroll
           for (int gg = 0; gg < D / 64; ++gg) {
@@ -539,7 +597,16 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) lm = min(lm, min(lim[nt][0], lim[nt][1]));
       lim_min = __reduce_min_sync(0xffffffffu, lm);
-      if constexpr (INT8) {
+      if constexpr (IMMA) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          // S fragment columns nt*8 + 2 q4 + e: their fixed-point scale, from a thread of that column
+#pragma unroll
+          for (int e = 0; e < 2; ++e) qs[nt][e] = __shfl_sync(0xffffffffu, qscale_own[nt], (2 * q4 + e) << 2);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc1[nt][c] = 0.f;
+        }
+      } else if constexpr (INT8) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           // this thread's Q fragments are column nt*8 + r; sum over the four
@@ -617,6 +684,41 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
             else mma16816<MMA_BF16>(s[mk][nt], a, qf[nt][kk][0], qf[nt][kk][1]);
           }
         }
+    } else if constexpr (IMMA) {
+      // raw int8 K rows r / r+8 as A, Q's hi / lo bytes as B: two exact int32 chains
+      int sh[KST][NT][4], sl[KST][NT][4];
+#pragma unroll
+      for (int mk = 0; mk < KST; ++mk)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sh[mk][nt][c] = sl[mk][nt][c] = 0;
+#pragma unroll
+      for (int gg = 0; gg < D / 64; ++gg) {
+        const int chn = 4 * gg + q4;
+#pragma unroll
+        for (int mk = 0; mk < KST; ++mk) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB, TK>(r + 16 * mk, chn));
+          const uint4 w1 = *reinterpret_cast<const uint4*>(kt + toff<C::ROWB, TK>(r + 8 + 16 * mk, chn));
+          const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t x1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int jj = 0; jj < 4; jj += 2) {
+            const uint32_t a[4] = {x0[jj], x1[jj], x0[jj + 1], x1[jj + 1]};
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              mma_s8_16832(sh[mk][nt], a, qf[nt][4 * gg + jj][0], qf[nt][4 * gg + jj + 1][0]);
+              mma_s8_16832(sl[mk][nt], a, qf[nt][4 * gg + jj][1], qf[nt][4 * gg + jj + 1][1]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int mk = 0; mk < KST; ++mk)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) s[mk][nt][c] = __int2float_rn(sh[mk][nt][c] * 256 + sl[mk][nt][c]);
     } else {
 #pragma unroll
       for (int gg = 0; gg < D / 64; ++gg) {
@@ -685,7 +787,8 @@ __global__ void __launch_bounds__(max_warps<NT>() * 32, 1)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             float sv = s[mk][nt][e + 2 * hh];
-            if constexpr (INT8) sv -= qs[nt][e];
+            if constexpr (IMMA) sv *= qs[nt][e];
+            else if constexpr (INT8) sv -= qs[nt][e];
             float v = sv * kscl[mk][hh];
             if (!full && key_r + 16 * mk + 8 * hh >= lim[nt][e]) v = -INFINITY;
             x[e][mk][hh] = v;

@@ -101,6 +101,18 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
   }
 }
 
+// D (int32) += A (16x32 s8, row) * B (32x8 s8, col), warp-level.  Thread
+// (group g, lane-in-group t) holds A rows g / g+8 at k = 4t..4t+3 (a0 / a1) and
+// 16+4t.. (a2 / a3), B column g at k = 4t.. (b0) and 16+4t.. (b1), four
+// int8 per register, the lowest k in the lowest byte.
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // ---------------------------------------------------------------------------
 // Scalar helpers.
 // ---------------------------------------------------------------------------
