@@ -250,12 +250,52 @@ bool make_pool_map(CUtensorMap* m, void* base, int dtype, int D, int H, int BS, 
   return r == CUDA_SUCCESS;
 }
 
-bool make_kv_maps(const pa_kv_cache_t* kv, pa::KvMaps* maps) {
-  if (std::getenv("PIE_B200_NO_TMA")) return false;
+bool encode_kv_maps(const pa_kv_cache_t* kv, pa::KvMaps* maps) {
   return make_pool_map(&maps->k, kv->k, kv->dtype, kv->head_dim, kv->num_kv_heads, kv->block_size, kv->num_blocks,
                        kv->k_stride_head, kv->k_stride_slot, kv->k_stride_block) &&
          make_pool_map(&maps->v, kv->v, kv->dtype, kv->head_dim, kv->num_kv_heads, kv->block_size, kv->num_blocks,
                        kv->v_stride_head, kv->v_stride_slot, kv->v_stride_block);
+}
+
+// The pool's TMA maps, remembered per thread for the last few pools: a decode
+// loop calls with the same pool every step, and encoding a map is a driver
+// call.  A map holds only the pool's address, shape and strides (the key).
+bool make_kv_maps(const pa_kv_cache_t* kv, pa::KvMaps* maps) {
+  static const bool no_tma = std::getenv("PIE_B200_NO_TMA") != nullptr;
+  if (no_tma) return false;
+  struct Entry {
+    pa_kv_cache_t key;
+    int dev;
+    pa::KvMaps maps;
+    bool ok;
+    bool used;
+  };
+  constexpr int kEntries = 4;
+  thread_local Entry cache[kEntries] = {};
+  thread_local int next = 0;
+  auto same = [&](const pa_kv_cache_t& a) {
+    return a.k == kv->k && a.v == kv->v && a.dtype == kv->dtype && a.num_blocks == kv->num_blocks &&
+           a.block_size == kv->block_size && a.num_kv_heads == kv->num_kv_heads && a.head_dim == kv->head_dim &&
+           a.k_stride_block == kv->k_stride_block && a.k_stride_slot == kv->k_stride_slot &&
+           a.k_stride_head == kv->k_stride_head && a.v_stride_block == kv->v_stride_block &&
+           a.v_stride_slot == kv->v_stride_slot && a.v_stride_head == kv->v_stride_head;
+  };
+  int dev = -1;
+  cudaGetDevice(&dev);
+  for (Entry& e : cache) {
+    if (e.used && e.dev == dev && same(e.key)) {
+      *maps = e.maps;
+      return e.ok;
+    }
+  }
+  Entry& e = cache[next];
+  next = (next + 1) % kEntries;
+  e.key = *kv;
+  e.dev = dev;
+  e.ok = encode_kv_maps(kv, &e.maps);
+  e.used = true;
+  *maps = e.maps;
+  return e.ok;
 }
 
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
