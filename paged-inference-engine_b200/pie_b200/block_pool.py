@@ -238,6 +238,23 @@ class DeviceBlockManager:
         return dict(block_table=bt, num_blocks_per_seq=nb, q_len=ql, kv_len=kl, cu_seqlens=cus, positions=pos,
                     token_seq=tseq)
 
+    def step_rows(self, seq_slot: torch.Tensor, q_len: torch.Tensor, kv_len: torch.Tensor, cu_seqlens: torch.Tensor,
+                  total_tokens: int, block_table: torch.Tensor, num_blocks: torch.Tensor, positions: torch.Tensor,
+                  token_seq: torch.Tensor, status: Optional[torch.Tensor] = None) -> None:
+        """``block_pool_step`` on caller-owned device tensors (no host copy, no allocation: capturable).
+
+        ``seq_slot`` / ``q_len`` / ``kv_len`` int32 [S], ``cu_seqlens`` [S + 1]; writes ``block_table``
+        [S, bt_cols] (row stride honoured), ``num_blocks`` [S], ``positions`` / ``token_seq`` [total_tokens].
+        """
+        S = seq_slot.numel()
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            _lib.check("block_pool_step", lib.block_pool_step(
+                ctypes.byref(self._desc), seq_slot.data_ptr(), q_len.data_ptr(), kv_len.data_ptr(),
+                cu_seqlens.data_ptr(), S, block_table.data_ptr(), block_table.stride(0), block_table.shape[1],
+                num_blocks.data_ptr(), positions.data_ptr(), token_seq.data_ptr(), int(total_tokens),
+                None if status is None else status.data_ptr(), self._stream()))
+
     @property
     def block_table(self) -> dict:
         """The per-sequence block lists as a host dict (reads the device: synchronises; for checks)."""
