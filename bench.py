@@ -21,9 +21,12 @@ with the reference's benchmark shapes (no public dataset is involved):
   prefill_bf16  causal paged prefill, B=8, L ~ U[1024, 4096], 32/8 heads, bf16;
                 K/V written into scattered fp16 blocks, then attention.
                 Metric: TFLOP/s (causal FLOPs).
+  prefill_int8  the same prefill over an INT8 pool (fp16 Q, quantise-on-write of
+                the new rows); the attention call dequantises the blocks it reads
+                once into fp16 scratch and runs the tcgen05 kernel.
 
 On one GPU the line also carries, under ``workloads``, a full record (value,
-roofline, e2e, clocks, cpu_baseline) for each of the other three workloads,
+roofline, e2e, clocks, cpu_baseline) for each of the other four workloads,
 timed the same way in the same run.  ``roofline`` describes the dominant
 launches: the attention call alone (no write kernel, no collective) on the
 same inputs, timed by a second CUDA-event loop after the timed region; its
@@ -342,14 +345,20 @@ class DecodeWorkload(Workload):
 
 
 class PrefillWorkload(Workload):
-    """prefill_bf16: B=8, L ~ U[1024, 4096], 32/8 heads, D=128, bf16; write K/V then attend."""
+    """prefill_bf16: B=8, L ~ U[1024, 4096], 32/8 heads, D=128, bf16; write K/V then attend.
+
+    prefill_int8: the same shape over an INT8 pool (fp16 Q and new rows, quantise-on-write with
+    head-major fp16 per-token scales); the attention call dequantises the blocks it reads once
+    into fp16 scratch, then runs the tcgen05 kernel.
+    """
 
     ROWS = 64  # query rows per CPU unit
 
-    def __init__(self, seed: int, device, cpu_only: bool = False):
+    def __init__(self, seed: int, device, cpu_only: bool = False, int8: bool = False):
         from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
 
-        self.name = "prefill_bf16"
+        self.int8 = int8
+        self.name = "prefill_int8" if int8 else "prefill_bf16"
         cfg = CONFIGS["prefill_bf16"]
         gen = torch.Generator().manual_seed(seed)
         L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
@@ -357,22 +366,29 @@ class PrefillWorkload(Workload):
         bt, nblk, NB = block_tables(gen, L, BS)
         maxL = max(L)
         self.L, self.BS, self.NB = L, BS, NB
-        self.Q = torch.randn(B, Hq, maxL, D, generator=gen).to(torch.bfloat16)
+        dt = torch.float16 if int8 else torch.bfloat16
+        self.Q = torch.randn(B, Hq, maxL, D, generator=gen).to(dt)
         T = sum(L)
-        self.kn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
-        self.vn = torch.randn(T, Hkv, D, generator=gen).to(torch.bfloat16)
+        self.kn = torch.randn(T, Hkv, D, generator=gen).to(dt)
+        self.vn = torch.randn(T, Hkv, D, generator=gen).to(dt)
         self.seq = torch.cat([torch.full((l,), i, dtype=torch.int32) for i, l in enumerate(L)])
         self.pos = torch.cat([torch.arange(l, dtype=torch.int32) for l in L])
         self.bt, self.nblk = bt, nblk
         self.Lt = torch.tensor(L, dtype=torch.int32)
         self.work = sum(4.0 * Hq * D * l * (l + 1) / 2 for l in L)
         self.dominant_work = self.work
-        self.info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS, "sum_len": T, "q_dtype": "bfloat16",
-                     "kv_dtype": "float16"}
-        self.unit, self.scale, self.bound, self.dtype = "TFLOP/s", 1e-12, "tensor", "bf16"
-        self.metric = "causal paged prefill TFLOP/s (bf16, B=8, L~U[1024,4096], 32/8 heads, D=128)"
-        self.kernel = "kv_write_copy + paged_attn_prefill"
-        self.dominant_name = "paged_attn_prefill (pa_prefill_tc2_kernel)"
+        self.info = {"B": B, "Hq": Hq, "Hkv": Hkv, "D": D, "block_size": BS, "sum_len": T,
+                     "q_dtype": "float16" if int8 else "bfloat16", "kv_dtype": "int8" if int8 else "float16"}
+        self.unit, self.scale, self.bound, self.dtype = "TFLOP/s", 1e-12, "tensor", "f16" if int8 else "bf16"
+        if int8:
+            self.metric = ("causal paged prefill TFLOP/s (INT8 KV pool, fp16 Q, B=8, L~U[1024,4096], 32/8 heads, "
+                           "D=128)")
+            self.kernel = "kv_write_quant + paged_attn_forward (kv_dequant_kernel + pa_prefill_tc2_kernel)"
+            self.dominant_name = "paged_attn_forward, INT8 pool (kv_dequant_kernel + pa_prefill_tc2_kernel)"
+        else:
+            self.metric = "causal paged prefill TFLOP/s (bf16, B=8, L~U[1024,4096], 32/8 heads, D=128)"
+            self.kernel = "kv_write_copy + paged_attn_prefill"
+            self.dominant_name = "paged_attn_prefill (pa_prefill_tc2_kernel)"
         self.launches = 2
         self.Hq, self.D = Hq, D
         if not cpu_only:
@@ -385,15 +401,23 @@ class PrefillWorkload(Workload):
         dev = [t.to(device) for t in host]
         Qd, knd, vnd, seqd, posd, btd, nbd, Ld = dev
         Hkv, D = self.kn.shape[1], self.kn.shape[2]
-        Kc = torch.empty(self.NB, self.BS, Hkv, D, dtype=torch.float16, device=device)
+        ks = vs = None
+        if self.int8:
+            from pie_b200.workloads import empty_head_major_scales
+
+            Kc = torch.empty(self.NB, self.BS, Hkv, D, dtype=torch.int8, device=device)
+            ks = empty_head_major_scales(self.NB, self.BS, Hkv, device=device)
+            vs = empty_head_major_scales(self.NB, self.BS, Hkv, device=device)
+        else:
+            Kc = torch.empty(self.NB, self.BS, Hkv, D, dtype=torch.float16, device=device)
         Vc = torch.empty_like(Kc)
-        self.dev = dict(Q=Qd, K=Kc, V=Vc, bt=btd, nb=nbd, L=Ld, kn=knd, vn=vnd, seq=seqd, pos=posd)
+        self.dev = dict(Q=Qd, K=Kc, V=Vc, ks=ks, vs=vs, bt=btd, nb=nbd, L=Ld, kn=knd, vn=vnd, seq=seqd, pos=posd)
 
         def attend(out=None):
-            return flash_attention_forward(Qd, Kc, Vc, Ld, btd, nbd, self.BS, Ld, None, None, out=out)
+            return flash_attention_forward(Qd, Kc, Vc, Ld, btd, nbd, self.BS, Ld, ks, vs, out=out)
 
         def step(out=None):
-            write_kv_cache(knd, vnd, btd, seqd, posd, Kc, Vc)
+            write_kv_cache(knd, vnd, btd, seqd, posd, Kc, Vc, ks, vs)
             return attend(out)
         self.step = step
         self.dominant = attend
@@ -406,8 +430,8 @@ class PrefillWorkload(Workload):
 
         def run(s, v):
             Q, kn, vn, seq, pos, bt, nb, Lx = v
-            write_kv_cache(kn, vn, bt, seq, pos, Kc, Vc)
-            O, _ = flash_attention_forward(Q, Kc, Vc, Lx, bt, nb, self.BS, Lx, None, None, out=outs[s])
+            write_kv_cache(kn, vn, bt, seq, pos, Kc, Vc, ks, vs)
+            O, _ = flash_attention_forward(Q, Kc, Vc, Lx, bt, nb, self.BS, Lx, ks, vs, out=outs[s])
             return O
 
         self.e2e_step = lambda: pipe.step(run)
@@ -417,16 +441,29 @@ class PrefillWorkload(Workload):
         # the copy-on-write of the new rows, done once (not timed)
         import numpy as np
 
+        from oracle import paged_attention as orc
+
         Hkv, D = self.kn.shape[1], self.kn.shape[2]
-        K = np.zeros((self.NB, self.BS, Hkv, D), np.float16)
-        V = np.zeros_like(K)
         seq, pos, bt = self.seq.numpy(), self.pos.numpy(), self.bt.numpy()
         blk = bt[seq, pos // self.BS]
-        K[blk, pos % self.BS] = self.kn.float().numpy().astype(np.float16)
-        V[blk, pos % self.BS] = self.vn.float().numpy().astype(np.float16)
+        ks = vs = None
+        if self.int8:
+            K = np.zeros((self.NB, self.BS, Hkv, D), np.int8)
+            V = np.zeros_like(K)
+            ks = np.ones((self.NB, self.BS, Hkv), np.float16)
+            vs = np.ones_like(ks)
+            for src, dst, sc in ((self.kn, K, ks), (self.vn, V, vs)):
+                q, s = orc.quantize_rows(src.float().numpy())
+                dst[blk, pos % self.BS] = q
+                sc[blk, pos % self.BS] = s.astype(np.float16)
+        else:
+            K = np.zeros((self.NB, self.BS, Hkv, D), np.float16)
+            V = np.zeros_like(K)
+            K[blk, pos % self.BS] = self.kn.float().numpy().astype(np.float16)
+            V[blk, pos % self.BS] = self.vn.float().numpy().astype(np.float16)
         units = [(b, lo) for b, l in enumerate(self.L) for lo in range(0, l, self.ROWS)]
         order = np.random.default_rng(0).permutation(len(units))
-        return K, V, [units[j] for j in order]
+        return K, V, ks, vs, [units[j] for j in order]
 
     def cpu_unit(self, i):
         """Query rows [lo, lo + ROWS) of one sequence against its causal keys."""
@@ -434,13 +471,14 @@ class PrefillWorkload(Workload):
 
         if not hasattr(self, "_cpu"):
             self._cpu = self._cpu_pool()
-        K, V, units = self._cpu
+        K, V, ks, vs, units = self._cpu
         b, lo = units[i % len(units)]
         l = self.L[b]
         hi = min(l, lo + self.ROWS)
         q = self.Q[b:b + 1, :, lo:hi].float().numpy()
         # bottom-right causal with kv_len = hi: row m (absolute lo + m) sees keys 0..lo+m
-        orc.paged_attention(q, K, V, [hi - lo], self.bt[b:b + 1].numpy(), self.nblk[b:b + 1].numpy(), self.BS, [hi])
+        orc.paged_attention(q, K, V, [hi - lo], self.bt[b:b + 1].numpy(), self.nblk[b:b + 1].numpy(), self.BS, [hi],
+                            ks, vs)
         return 4.0 * self.Hq * self.D * sum(r + 1 for r in range(lo, hi))
 
     def sample_desc(self, n, t):
@@ -539,8 +577,8 @@ class LongCtxWorkload(Workload):
 
 def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl",
                   batch: int = 0) -> Workload:
-    if name == "prefill_bf16":
-        return PrefillWorkload(1000 + rank, device, cpu_only)
+    if name in ("prefill_bf16", "prefill_int8"):
+        return PrefillWorkload(1000 + rank, device, cpu_only, int8=name == "prefill_int8")
     if name == "long_ctx_int8":
         return LongCtxWorkload(ws, rank, device, cpu_only, exchange, batch)
     return DecodeWorkload(name, 1000 + rank, device, cpu_only)
@@ -643,7 +681,7 @@ def measure(w: Workload, a, device, ws: int, rank: int, local: int, peaks: dict,
     return rec
 
 
-EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16")
+EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8")
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -682,18 +720,23 @@ def reference_kernel_leg(w: Workload, a, device) -> dict:
     except Exception as e:  # noqa: BLE001
         return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     try:
-        if w.name == "prefill_bf16":
+        if w.name.startswith("prefill"):
             d = w.dev
             from kernels.flash_attention import write_kv_cache
 
-            write_kv_cache(d["kn"], d["vn"], d["bt"], d["seq"], d["pos"], d["K"], d["V"])
+            write_kv_cache(d["kn"], d["vn"], d["bt"], d["seq"], d["pos"], d["K"], d["V"], d["ks"], d["vs"])
             G = d["Q"].shape[1] // d["K"].shape[2]
             Q = d["Q"].float()
             Kx = d["K"].repeat_interleave(G, dim=2)
             Vx = d["V"].repeat_interleave(G, dim=2)
-            ones = torch.ones(Kx.shape[0], Kx.shape[2], dtype=torch.float32, device=device)
-            args = (Q, Kx, Vx, d["L"], d["bt"], d["nb"], w.BS, d["L"], ones, ones)
-            note = "prefill rows (q_len = kv_len), K/V heads expanded x4, float32 Q"
+            if d["ks"] is not None:
+                ks = d["ks"].float().amax(dim=1).repeat_interleave(G, dim=1).contiguous()
+                vs = d["vs"].float().amax(dim=1).repeat_interleave(G, dim=1).contiguous()
+                note = "prefill rows (q_len = kv_len), INT8 pool with per-(block, head) scales, heads expanded x4"
+            else:
+                ks = vs = torch.ones(Kx.shape[0], Kx.shape[2], dtype=torch.float32, device=device)
+                note = "prefill rows (q_len = kv_len), K/V heads expanded x4, float32 Q"
+            args = (Q, Kx, Vx, d["L"], d["bt"], d["nb"], w.BS, d["L"], ks, vs)
         else:
             g = w.g
             G = g.Q.shape[1] // g.K.shape[2]
@@ -739,7 +782,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="long_ctx_int8",
-                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "long_ctx_int8"])
+                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8", "long_ctx_int8"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",

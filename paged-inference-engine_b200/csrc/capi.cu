@@ -410,10 +410,77 @@ bool make_q_map(CUtensorMap* m, const pa_attn_io_t* io, int D, int B, int q_tota
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, const pa_attn_io_t* io, void* stream) {
+// Scratch of an INT8 prefill on the tcgen05 kernel: the blocks the call reads,
+// dequantised to fp16 (see kv_dequant.cu).  gather when the call's table holds
+// fewer blocks than the pool (then a scratch block table too), else a mirror
+// of the whole pool.  0 when the tcgen05 kernel cannot take the problem or the
+// scratch would exceed kMaxDequantScratch (the mma.sync kernel then reads the
+// int8 pool directly).
+constexpr size_t kMaxDequantScratch = static_cast<size_t>(16) << 30;
+struct DequantLayout {
+  size_t dk, dv, dbt, total;
+  long long blocks;
+  bool gather;
+};
+DequantLayout dequant_layout(const pa::AttnParams& p, const pa_kv_cache_t* kv) {
+  DequantLayout l{};
+  if (kv->dtype != PA_DTYPE_I8 || !pa::prefill_tc_supported(pa::KV_F16, kv->head_dim, kv->block_size) ||
+      std::getenv("PIE_B200_NO_TCGEN05"))
+    return l;
+  const long long table_blocks = static_cast<long long>(p.B) * p.bt_cols;
+  l.gather = table_blocks <= kv->num_blocks;
+  l.blocks = l.gather ? table_blocks : kv->num_blocks;
+  const size_t pool = align256(static_cast<size_t>(l.blocks) * kv->block_size * kv->num_kv_heads * kv->head_dim * 2);
+  l.dk = 0;
+  l.dv = pool;
+  l.dbt = 2 * pool;
+  l.total = l.dbt + (l.gather ? align256(static_cast<size_t>(table_blocks) * 4) : 0);
+  if (l.blocks == 0 || l.total > kMaxDequantScratch) l = DequantLayout{};
+  return l;
+}
+
+int run_prefill(pa::AttnParams& p, const pa_kv_cache_t* kv, const pa_attn_io_t* io, void* stream,
+                void* ws = nullptr, size_t ws_bytes = 0) {
   if (p.B == 0 || p.maxq == 0) return PA_OK;
   if (p.B > 65535) return fail(PA_ERR_UNSUPPORTED, "prefill kernel supports at most 65535 sequences per call");
   const int kvk = kv_kind(kv->dtype);
+  const DequantLayout dq = dequant_layout(p, kv);
+  if (dq.total && ws && ws_bytes >= dq.total && al(ws, 256) && al(io->o, 16) && row_al(io->o_stride_seq, 2, 16) &&
+      row_al(io->o_stride_head, 2, 16) && row_al(io->o_stride_row, 2, 16)) {
+    // INT8 pool: dequantise the blocks the call reads once, then the fp16 tcgen05 kernel over them
+    char* base = static_cast<char*>(ws);
+    __half* dk = reinterpret_cast<__half*>(base + dq.dk);
+    __half* dv = reinterpret_cast<__half*>(base + dq.dv);
+    int* dbt = dq.gather ? reinterpret_cast<int*>(base + dq.dbt) : nullptr;
+    cudaError_t e = pa::launch_kv_dequant(p, dk, dv, dbt, dq.gather ? 1 : 0, kv->head_dim,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "INT8 prefill dequantisation launch");
+    pa_kv_cache_t f = *kv;
+    f.k = dk;
+    f.v = dv;
+    f.dtype = PA_DTYPE_F16;
+    f.num_blocks = static_cast<int32_t>(dq.blocks);
+    f.k_stride_head = f.v_stride_head = kv->head_dim;
+    f.k_stride_slot = f.v_stride_slot = static_cast<int64_t>(kv->num_kv_heads) * kv->head_dim;
+    f.k_stride_block = f.v_stride_block = static_cast<int64_t>(kv->block_size) * kv->num_kv_heads * kv->head_dim;
+    f.k_scale = f.v_scale = nullptr;
+    pa::AttnParams q = p;
+    fill_cache(q, &f);
+    q.status = p.status;
+    if (dq.gather) {
+      q.bt = dbt;
+      q.bt_ss = p.bt_cols;
+      q.bt_sc = 1;
+    }
+    pa::KvMaps maps;
+    CUtensorMap qmap;
+    if (make_kv_maps(&f, &maps) && make_q_map(&qmap, io, kv->head_dim, p.B, p.q_start ? p.q_total : 0)) {
+      e = pa::launch_prefill_tc(q, maps.k, maps.v, qmap, pa::KV_F16, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "prefill (tcgen05, dequantised INT8) launch");
+      return PA_OK;
+    }
+    return fail(PA_ERR_CUDA, "could not encode the TMA maps of the dequantised INT8 pool");
+  }
   if (pa::prefill_tc_supported(kvk, kv->head_dim, kv->block_size) && !std::getenv("PIE_B200_NO_TCGEN05") &&
       al(io->o, 16) && row_al(io->o_stride_seq, 2, 16) && row_al(io->o_stride_head, 2, 16) &&
       row_al(io->o_stride_row, 2, 16)) {
@@ -538,7 +605,11 @@ int paged_attn_workspace_size(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   pa::AttnParams p;
   int rc = build_attn(io, kv, pg, nullptr, p);
   if (rc) return rc;
-  if (!use_decode(p, kv) || p.B == 0 || p.maxq == 0) return PA_OK;
+  if (p.B == 0 || p.maxq == 0) return PA_OK;
+  if (!use_decode(p, kv)) {
+    *bytes = dequant_layout(p, kv).total;  // 0 unless an INT8 pool takes the tcgen05 prefill
+    return PA_OK;
+  }
   const int per_launch = p.B < kMaxDecodeSeqs ? p.B : kMaxDecodeSeqs;
   pa::KvMaps maps;
   const bool tma = make_kv_maps(kv, &maps);
@@ -556,7 +627,7 @@ int paged_attn_forward(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa
   int rc = build_attn(io, kv, pg, status, p);
   if (rc) return rc;
   if (use_decode(p, kv)) return run_decode(p, kv, workspace, workspace_bytes, stream);
-  return run_prefill(p, kv, io, stream);
+  return run_prefill(p, kv, io, stream, workspace, workspace_bytes);
 }
 
 int paged_attn_decode(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_paging_t* pg, void* workspace,
@@ -598,7 +669,7 @@ int paged_attn_varlen(const pa_attn_io_t* io, const pa_kv_cache_t* kv, const pa_
   p.q_start = q_start;
   p.q_total = total_q_rows;
   if (use_decode(p, kv)) return run_decode(p, kv, workspace, workspace_bytes, stream);
-  return run_prefill(p, kv, io, stream);
+  return run_prefill(p, kv, io, stream, workspace, workspace_bytes);
 }
 
 int paged_attn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {

@@ -4,6 +4,7 @@
 
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "paged_attn_b200.h"
@@ -170,6 +171,10 @@ cudaError_t launch_peer_barrier(int* local_flags, const PeerFlags& peers, int n,
 cudaError_t launch_decode(const AttnParams& p, const KvMaps* maps, int kv_kind, int q_bf16, int D, int nt,
                           const DecodeLaunch& plan, cudaStream_t stream, int phase = DECODE_BOTH);
 cudaError_t launch_prefill(const AttnParams& p, int kv_kind, int D, int mma_bf16, cudaStream_t stream);
+// INT8 blocks of a prefill call -> fp16 scratch pool (gather: block (b, j) to b * bt_cols + j with the
+// matching table written to dbt; mirror: block x to x).
+cudaError_t launch_kv_dequant(const AttnParams& p, __half* dk, __half* dv, int* dbt, int gather, int D,
+                              cudaStream_t stream);
 // tcgen05/TMEM prefill (16-bit pools, head_dim 128, block_size >= 8).
 bool prefill_tc_supported(int kv_kind, int D, int BS);
 cudaError_t launch_prefill_tc(const AttnParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
