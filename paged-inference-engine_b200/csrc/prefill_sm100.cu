@@ -495,7 +495,7 @@ constexpr int P2_XCH = P2_BAR + 256;              // float [2 heads][128 rows]
 constexpr int P2_SMEM = P2_XCH + 1024 + 1024;      // + alignment slack
 static_assert(P2_SMEM <= 227 * 1024, "shared memory per CTA");
 
-template <bool MMA_BF16, bool Q_CONVERT>
+template <bool MMA_BF16, bool Q_CONVERT, bool QUART>
 __global__ void __launch_bounds__(P2_THREADS, 1)
     pa_prefill_tc2_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
   pdl_enter();
@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(C_SFULL + x), 1);
-      mbar_init(bar(C_PFULL + x), 256);
+      mbar_init(bar(C_PFULL + x), QUART ? 512 : 256);
       mbar_init(bar(C_ODONE + x), 1);
     }
     fence_mbar_init();
@@ -649,6 +649,177 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
           qk(1, j + 1);
           tc_commit(bar(C_KEMPTY + (j + 1) % P2_KS));
         }
+      }
+    }
+  } else if constexpr (QUART) {
+    // ------------------------------------------------------------ softmax (warps 0-15), one head at a time
+    // Warp w serves TMEM lanes 32 (w % 4) .. (rows) and the keys [32 qt, 32 qt + 32) of every tile,
+    // qt = w / 4, and does head a, then head b, of every tile: all 16 warps (four per sub-partition)
+    // work on one head while the tensor core runs the other head's P*V and next Q*K^T.  The four
+    // quarters of a row combine their maxima through shared memory (as fp16: every quarter rounds
+    // and compares the same values, so all use the same reference max; P and the row sum are
+    // relative to it, which the final division and the LSE undo).
+    const int lg = warp & 3;        // lane group: TMEM lanes / rows 32 lg ..
+    const int qt = warp >> 2;       // key quarter of every tile
+    const int r = tid & 127;        // query row within the tile = TMEM lane
+    const int row = m0 + r;
+    const int gbar = 1 + lg;        // named barrier of the lane group's four warps (128 threads)
+    const uint32_t trow = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    __half* xq = reinterpret_cast<__half*>(sm + P2_XCH);  // [4 quarters][128 rows]
+    if (nt > 0) {
+      wait_or_flag(p, bar(C_QFULL), 0);
+      if constexpr (Q_CONVERT) {
+        uint4* q4 = reinterpret_cast<uint4*>(sm + P2_QA);
+#pragma unroll 4
+        for (int i = tid; i < 2 * TILE_B / 16; i += 512) {
+          uint4 v = q4[i];
+          v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
+          v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
+          v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
+          v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
+          q4[i] = v;
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar(C_QREADY));
+    }
+    const int lim = min(nkeys, off + row + 1);
+    float m_ref[2] = {-INFINITY, -INFINITY};
+    float l[2] = {0.f, 0.f};
+    const float c2 = p.scale_log2;
+    for (int j = 0; j < nt; ++j) {
+      const int k0 = j * TC_BN + 32 * qt;  // first key of this quarter
+      const bool need_mask = (k0 + 32 > off + m0 + 1) || (k0 + 32 > nkeys);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const uint32_t scol = s_col(x);
+        wait_or_flag(p, bar(C_SFULL + x), j & 1);
+        tc_fence_after();
+        uint32_t rr[32];
+        tmem_ld32(trow + scol + 32 * qt, rr);
+        tmem_wait_ld();
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float v = (k0 + i < lim) ? __uint_as_float(rr[i]) : -INFINITY;
+            rr[i] = __float_as_uint(v);
+            mx4[i & 3] = fmaxf(mx4[i & 3], v);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(rr[i]), __uint_as_float(rr[i + 1]));
+        }
+        // the row's maximum over the four quarters (also orders every quarter's S load before any P store)
+        xq[qt * 128 + r] = __float2half_ru(fminf(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), 65504.f));
+        named_barrier_sync(gbar, 128);
+        const float mrow = fmaxf(fmaxf(__half2float(xq[r]), __half2float(xq[128 + r])),
+                                 fmaxf(__half2float(xq[256 + r]), __half2float(xq[384 + r])));
+        named_barrier_sync(gbar, 128);  // every quarter has read before the next head's post
+        const float mx = mrow * c2;
+        float alpha = 1.f;
+        bool resc = false;
+        if (mx > m_ref[x] + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
+          alpha = ex2(m_ref[x] - mx);
+          resc = j > 0;
+          m_ref[x] = mx;
+        }
+        const float neg_m = (m_ref[x] == -INFINITY) ? 0.f : -m_ref[x];
+        // P of keys [32 qt, 32 qt + 32) goes to TMEM columns [16 qt, 16 qt + 16) of S_x
+        uint64_t lsum2 = f2_pack(0.f, 0.f);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float p0, p1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                           f2_pack(neg_m, neg_m)),
+                    p0, p1);
+          p0 = ex2(p0);
+          p1 = ex2(p1);
+          if (need_mask) {
+            const int kk = k0 + 2 * i;
+            if (kk >= lim) p0 = 0.f;
+            if (kk + 1 >= lim) p1 = 0.f;
+          }
+          lsum2 = f2_add(lsum2, f2_pack(p0, p1));
+          pk[i] = pack2<MMA_BF16>(p0, p1);
+        }
+        tmem_st16(trow + scol + 16 * qt, pk);
+        {
+          float a0, a1;
+          f2_unpack(lsum2, a0, a1);
+          l[x] = l[x] * alpha + (a0 + a1);
+        }
+        // O holds P*V(<j) complete (S_x(j) ready implies P*V_x(j-1) done): rescale this quarter of the row
+        if (__any_sync(0xffffffffu, resc)) {
+          const float a = resc ? alpha : 1.f;
+          uint32_t oo[32];
+          tmem_ld32(trow + O_COL + 128 * x + 32 * qt, oo);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) oo[i] = __float_as_uint(__uint_as_float(oo[i]) * a);
+          tmem_st32(trow + O_COL + 128 * x + 32 * qt, oo);
+        }
+        tmem_wait_st();
+        const int kt = j * TC_BN;
+        if (x == 0 && nkeys - kt < TC_BN) {
+          // keys past the sequence: zero their V rows (head a's P*V runs first); this quarter
+          // zeroes 64 bytes of the row: half qt >> 1, bytes 64 (qt & 1) ..
+          wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
+          if (kt + r >= nkeys) {
+            unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + (qt >> 1) * HALF_B + r * 128 + 64 * (qt & 1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        mbar_arrive(bar(C_PFULL + x));
+      }
+    }
+    // ---- epilogue: O / l, LSE (the row sum is the sum of the four quarters' sums) ------------
+    // The K ring is free once the last P*V of head a has completed (every Q*K^T was issued
+    // before it); the four quarters exchange their sums there.
+    float* lx = reinterpret_cast<float*>(sm + P2_K);  // [2 heads][4 quarters][128 rows]
+    if (nt > 0) {
+      wait_or_flag(p, bar(C_ODONE + 0), (nt - 1) & 1);
+      wait_or_flag(p, bar(C_ODONE + 1), (nt - 1) & 1);
+      tc_fence_after();
+    }
+#pragma unroll
+    for (int x = 0; x < 2; ++x) lx[(x * 4 + qt) * 128 + r] = l[x];
+    named_barrier_sync(gbar, 128);
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const float lt = (lx[(x * 4 + 0) * 128 + r] + lx[(x * 4 + 1) * 128 + r]) +
+                       (lx[(x * 4 + 2) * 128 + r] + lx[(x * 4 + 3) * 128 + r]);
+      const int hq = hq0 + x;
+      const bool valid = row < qlen;
+      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh +
+                     static_cast<long long>(row) * p.o_sm + 32 * qt;
+      if (nt > 0) {
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        uint32_t oo[32];
+        tmem_ld32(trow + O_COL + 128 * x + 32 * qt, oo);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_f16(__uint_as_float(oo[8 * v + 0]) * inv, __uint_as_float(oo[8 * v + 1]) * inv);
+            w.y = pack_f16(__uint_as_float(oo[8 * v + 2]) * inv, __uint_as_float(oo[8 * v + 3]) * inv);
+            w.z = pack_f16(__uint_as_float(oo[8 * v + 4]) * inv, __uint_as_float(oo[8 * v + 5]) * inv);
+            w.w = pack_f16(__uint_as_float(oo[8 * v + 6]) * inv, __uint_as_float(oo[8 * v + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + 8 * v) = w;
+          }
+        }
+      } else if (valid) {
+        for (int d = 0; d < 32; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+      }
+      if (valid && p.lse && qt == 0) {
+        const float L = lt > 0.f ? (m_ref[x] + lg2(lt)) * 0.6931471805599453f : -INFINITY;
+        static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+            __float2half_rn(L);
       }
     }
   } else {
@@ -875,9 +1046,19 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
       if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
+    static const bool halves = std::getenv("PIE_B200_TC_HALVES") != nullptr;
+    if (!halves) {
+      if (mma_bf16)
+        return convert ? launch2(pa_prefill_tc2_kernel<true, true, true>)
+                       : launch2(pa_prefill_tc2_kernel<true, false, true>);
+      return convert ? launch2(pa_prefill_tc2_kernel<false, true, true>)
+                     : launch2(pa_prefill_tc2_kernel<false, false, true>);
+    }
     if (mma_bf16)
-      return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
-    return convert ? launch2(pa_prefill_tc2_kernel<false, true>) : launch2(pa_prefill_tc2_kernel<false, false>);
+      return convert ? launch2(pa_prefill_tc2_kernel<true, true, false>)
+                     : launch2(pa_prefill_tc2_kernel<true, false, false>);
+    return convert ? launch2(pa_prefill_tc2_kernel<false, true, false>)
+                   : launch2(pa_prefill_tc2_kernel<false, false, false>);
   }
   const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);
   auto launch = [&](auto kern) {
