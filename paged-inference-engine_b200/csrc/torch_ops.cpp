@@ -13,6 +13,8 @@
 // TORCH_CHECK failure (RuntimeError) carrying paged_attn_error_string().  The
 // split-K workspace is one cached uint8 tensor per device from torch's
 // allocator, grown on demand.  Meta kernels give shapes for fake tensors.
+// Malformed arguments raise ValueError (TORCH_CHECK_VALUE), as the Python
+// front end does; a failing library call raises RuntimeError.
 //
 // Pools arrive as [num_blocks, block_size, num_kv_heads, head_dim] views (the
 // launcher's [block, slot, head, d] reading, kernels/flash_attention.py:158-159);
@@ -42,7 +44,7 @@ int pa_dtype(at::ScalarType t) {
     case at::kFloat:
       return PA_DTYPE_F32;
     default:
-      TORCH_CHECK(false, "pie_b200: unsupported dtype ", t);
+      TORCH_CHECK_VALUE(false, "pie_b200: unsupported dtype ", t);
   }
   return -1;
 }
@@ -58,18 +60,18 @@ T* opt_ptr(const std::optional<at::Tensor>& t) {
 }
 
 void check_device(const at::Tensor& ref, const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.device() == ref.device(), "pie_b200: ", name, " must be on ", ref.device());
+  TORCH_CHECK_VALUE(t.is_cuda() && t.device() == ref.device(), "pie_b200: ", name, " must be on ", ref.device());
 }
 void check_i32(const at::Tensor& ref, const at::Tensor& t, const char* name, int64_t n) {
   check_device(ref, t, name);
-  TORCH_CHECK(t.scalar_type() == at::kInt && t.dim() == 1 && t.is_contiguous(), "pie_b200: ", name,
+  TORCH_CHECK_VALUE(t.scalar_type() == at::kInt && t.dim() == 1 && t.is_contiguous(), "pie_b200: ", name,
               " must be a contiguous int32 vector");
-  TORCH_CHECK(t.numel() == n, "pie_b200: ", name, " has ", t.numel(), " entries, expected ", n);
+  TORCH_CHECK_VALUE(t.numel() == n, "pie_b200: ", name, " has ", t.numel(), " entries, expected ", n);
 }
 
 pa_kv_cache_t kv_desc(const at::Tensor& K, const at::Tensor& V, const std::optional<at::Tensor>& ks,
                       const std::optional<at::Tensor>& vs) {
-  TORCH_CHECK(K.dim() == 4 && V.dim() == 4 && K.sizes() == V.sizes() && K.scalar_type() == V.scalar_type(),
+  TORCH_CHECK_VALUE(K.dim() == 4 && V.dim() == 4 && K.sizes() == V.sizes() && K.scalar_type() == V.scalar_type(),
               "pie_b200: K and V pools must be 4-D [num_blocks, block_size, num_kv_heads, head_dim] and alike");
   check_device(K, V, "V");
   pa_kv_cache_t kv{};
@@ -80,7 +82,7 @@ pa_kv_cache_t kv_desc(const at::Tensor& K, const at::Tensor& V, const std::optio
   kv.block_size = static_cast<int32_t>(K.size(1));
   kv.num_kv_heads = static_cast<int32_t>(K.size(2));
   kv.head_dim = static_cast<int32_t>(K.size(3));
-  TORCH_CHECK(K.stride(3) == 1 && V.stride(3) == 1, "pie_b200: K/V pools need a contiguous head_dim");
+  TORCH_CHECK_VALUE(K.stride(3) == 1 && V.stride(3) == 1, "pie_b200: K/V pools need a contiguous head_dim");
   kv.k_stride_block = K.stride(0);
   kv.k_stride_slot = K.stride(1);
   kv.k_stride_head = K.stride(2);
@@ -89,27 +91,27 @@ pa_kv_cache_t kv_desc(const at::Tensor& K, const at::Tensor& V, const std::optio
   kv.v_stride_head = V.stride(2);
   kv.scale_dtype = PA_DTYPE_F16;
   if (kv.dtype == PA_DTYPE_I8) {
-    TORCH_CHECK(ks.has_value() && vs.has_value(), "pie_b200: an int8 KV pool needs k_scale and v_scale");
+    TORCH_CHECK_VALUE(ks.has_value() && vs.has_value(), "pie_b200: an int8 KV pool needs k_scale and v_scale");
     const at::Tensor* sc[2] = {&*ks, &*vs};
     int64_t st[2][3];
     for (int i = 0; i < 2; ++i) {
       const at::Tensor& s = *sc[i];
       check_device(K, s, i ? "v_scale" : "k_scale");
       if (s.dim() == 2) {
-        TORCH_CHECK(s.size(0) == K.size(0) && s.size(1) == K.size(2), "pie_b200: per-block scales must be [",
+        TORCH_CHECK_VALUE(s.size(0) == K.size(0) && s.size(1) == K.size(2), "pie_b200: per-block scales must be [",
                     K.size(0), ", ", K.size(2), "]");
         st[i][0] = s.stride(0);
         st[i][1] = 0;
         st[i][2] = s.stride(1);
       } else {
-        TORCH_CHECK(s.dim() == 3 && s.size(0) == K.size(0) && s.size(1) == K.size(1) && s.size(2) == K.size(2),
+        TORCH_CHECK_VALUE(s.dim() == 3 && s.size(0) == K.size(0) && s.size(1) == K.size(1) && s.size(2) == K.size(2),
                     "pie_b200: per-token scales must be [", K.size(0), ", ", K.size(1), ", ", K.size(2), "]");
         st[i][0] = s.stride(0);
         st[i][1] = s.stride(1);
         st[i][2] = s.stride(2);
       }
     }
-    TORCH_CHECK(ks->scalar_type() == vs->scalar_type() &&
+    TORCH_CHECK_VALUE(ks->scalar_type() == vs->scalar_type() &&
                     (ks->scalar_type() == at::kHalf || ks->scalar_type() == at::kFloat),
                 "pie_b200: k_scale / v_scale must share a float16 or float32 dtype");
     kv.scale_dtype = pa_dtype(ks->scalar_type());
@@ -128,7 +130,7 @@ pa_kv_cache_t kv_desc(const at::Tensor& K, const at::Tensor& V, const std::optio
 pa_paging_t paging(const at::Tensor& ref, const at::Tensor& block_table, const at::Tensor& num_blocks,
                    const at::Tensor& q_len, const at::Tensor& kv_len) {
   check_device(ref, block_table, "block_table");
-  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2,
+  TORCH_CHECK_VALUE(block_table.scalar_type() == at::kInt && block_table.dim() == 2,
               "pie_b200: block_table must be int32 [num_seqs, max_blocks]");
   const int64_t B = block_table.size(0);
   check_i32(ref, num_blocks, "num_blocks_per_seq", B);
@@ -197,16 +199,16 @@ pa_attn_io_t io_desc(const at::Tensor& Q, const at::Tensor& O, const at::Tensor&
 }
 
 void check_q(const at::Tensor& Q, int64_t dims) {
-  TORCH_CHECK(Q.is_cuda() && Q.dim() == dims, "pie_b200: Q must be a ", dims, "-D CUDA tensor");
-  TORCH_CHECK(Q.scalar_type() == at::kHalf || Q.scalar_type() == at::kBFloat16, "pie_b200: Q must be fp16 or bf16");
-  TORCH_CHECK(Q.stride(dims - 1) == 1, "pie_b200: Q needs a contiguous head_dim");
+  TORCH_CHECK_VALUE(Q.is_cuda() && Q.dim() == dims, "pie_b200: Q must be a ", dims, "-D CUDA tensor");
+  TORCH_CHECK_VALUE(Q.scalar_type() == at::kHalf || Q.scalar_type() == at::kBFloat16, "pie_b200: Q must be fp16 or bf16");
+  TORCH_CHECK_VALUE(Q.stride(dims - 1) == 1, "pie_b200: Q needs a contiguous head_dim");
 }
 
 void check_out(const at::Tensor& Q, const at::Tensor& O, const at::Tensor& L) {
   check_device(Q, O, "out");
   check_device(Q, L, "lse");
-  TORCH_CHECK(O.scalar_type() == at::kHalf && O.sizes() == Q.sizes(), "pie_b200: out must be float16 shaped like Q");
-  TORCH_CHECK(L.scalar_type() == at::kHalf && L.sizes() == Q.sizes().slice(0, Q.dim() - 1),
+  TORCH_CHECK_VALUE(O.scalar_type() == at::kHalf && O.sizes() == Q.sizes(), "pie_b200: out must be float16 shaped like Q");
+  TORCH_CHECK_VALUE(L.scalar_type() == at::kHalf && L.sizes() == Q.sizes().slice(0, Q.dim() - 1),
               "pie_b200: lse must be float16 shaped like Q without head_dim");
 }
 
@@ -218,7 +220,8 @@ void paged_attention_out(const at::Tensor& Q, const at::Tensor& K, const at::Ten
                          const std::optional<at::Tensor>& status, at::Tensor& out, at::Tensor& lse) {
   check_q(Q, 4);
   check_out(Q, out, lse);
-  TORCH_CHECK(block_table.size(0) == Q.size(0), "pie_b200: block_table has ", block_table.size(0), " rows for ",
+  check_device(Q, K, "K");
+  TORCH_CHECK_VALUE(block_table.size(0) == Q.size(0), "pie_b200: block_table has ", block_table.size(0), " rows for ",
               Q.size(0), " sequences");
   const c10::cuda::CUDAGuard guard(Q.device());
   pa_kv_cache_t kv = kv_desc(K, V, k_scale, v_scale);
@@ -262,6 +265,7 @@ void paged_attention_varlen_out(const at::Tensor& Q, const at::Tensor& q_start, 
                                 at::Tensor& out, at::Tensor& lse) {
   check_q(Q, 3);
   check_out(Q, out, lse);
+  check_device(Q, K, "K");
   const c10::cuda::CUDAGuard guard(Q.device());
   pa_kv_cache_t kv = kv_desc(K, V, k_scale, v_scale);
   pa_paging_t pg = paging(Q, block_table, num_blocks, q_len, kv_len);
@@ -294,13 +298,13 @@ void write_kv(const at::Tensor& k_new, const at::Tensor& v_new, const at::Tensor
               const at::Tensor& seq_index, const at::Tensor& positions, at::Tensor& k_cache, at::Tensor& v_cache,
               const std::optional<at::Tensor>& k_scale, const std::optional<at::Tensor>& v_scale,
               const std::optional<at::Tensor>& status) {
-  TORCH_CHECK(k_new.dim() == 3 && v_new.sizes() == k_new.sizes() && v_new.scalar_type() == k_new.scalar_type(),
+  TORCH_CHECK_VALUE(k_new.dim() == 3 && v_new.sizes() == k_new.sizes() && v_new.scalar_type() == k_new.scalar_type(),
               "pie_b200: k_new / v_new must be [num_tokens, num_kv_heads, head_dim] of equal shape and dtype");
-  TORCH_CHECK(k_new.stride(2) == 1 && v_new.stride(2) == 1, "pie_b200: new rows need a contiguous head_dim");
+  TORCH_CHECK_VALUE(k_new.stride(2) == 1 && v_new.stride(2) == 1, "pie_b200: new rows need a contiguous head_dim");
   check_device(k_cache, k_new, "k_new");
   check_device(k_cache, v_new, "v_new");
   check_device(k_cache, block_table, "block_table");
-  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2, "pie_b200: block_table must be int32 2-D");
+  TORCH_CHECK_VALUE(block_table.scalar_type() == at::kInt && block_table.dim() == 2, "pie_b200: block_table must be int32 2-D");
   const int64_t T = k_new.size(0);
   check_i32(k_cache, seq_index, "seq_index", T);
   check_i32(k_cache, positions, "positions", T);

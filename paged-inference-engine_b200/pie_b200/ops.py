@@ -14,6 +14,7 @@ two paths launch the same kernels with the same arguments.
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from typing import Optional
 
@@ -40,6 +41,25 @@ def _torch_ops():
     from . import _torch_ext
 
     return _torch_ext.ops()
+
+
+_OPS: dict = {}
+
+
+def _op(name: str):
+    """The registered op's default overload, looked up once (a direct call skips the packet dispatch)."""
+    op = _OPS.get(name)
+    if op is None:
+        op = getattr(_torch_ops(), name).default
+        _OPS[name] = op
+    return op
+
+
+def _out_and_lse(shape: tuple, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """O (shape) and LSE (shape without head_dim), float16, from one allocation (O first, 256-byte aligned)."""
+    n_o = math.prod(shape)
+    buf = torch.empty(n_o + math.prod(shape[:-1]), dtype=torch.float16, device=device)
+    return buf[:n_o].view(shape), buf[n_o:].view(shape[:-1])
 
 
 def _i32(t: torch.Tensor) -> torch.Tensor:
@@ -228,20 +248,17 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
         raise ValueError(f"block_size {block_size} does not match the pool's slot dimension {K.shape[1]}")
     if K.shape[3] != D:
         raise ValueError(f"head_dim of Q ({D}) and of the pool ({K.shape[3]}) differ")
-    dev = Q.device
-    for name, t in (("K", K), ("V", V), ("block_table", block_table), ("q_len_per_seq", q_len_per_seq),
-                    ("kv_len_per_seq", kv_len_per_seq), ("num_blocks_per_seq", num_blocks_per_seq)):
-        if t.device != dev:
-            raise ValueError(f"{name} is on {t.device}, Q on {dev}")
     if block_table.shape[0] != B:
         raise ValueError(f"block_table has {block_table.shape[0]} rows for {B} sequences")
-    mma_dtype = K.dtype if K.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    dev = Q.device
     if Q.dtype not in (torch.float16, torch.bfloat16):
-        Q = Q.to(mma_dtype)
+        Q = Q.to(K.dtype if K.dtype in (torch.float16, torch.bfloat16) else torch.float16)
     if Q.stride(3) != 1:
         Q = Q.contiguous()
     if mode not in _MODES:
         raise ValueError(f"mode must be one of {sorted(_MODES)}, not {mode!r}")
+    if out is None and lse is None:
+        out, lse = _out_and_lse((B, Hq, maxq, D), dev)
     if out is None:
         out = torch.empty((B, Hq, maxq, D), dtype=torch.float16, device=dev)
     elif out.dtype != torch.float16 or tuple(out.shape) != (B, Hq, maxq, D):
@@ -251,14 +268,18 @@ def paged_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per
     if status is None and _CHECK:
         status = status_word(dev)
     if BACKEND == "torch":
-        check_cache(K, V, k_scale, v_scale)
-        bt, nbk, ql, kl = _paging_tensors(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq)
-        _torch_ops().paged_attention_out(Q, K, V, ql, bt, nbk, kl, k_scale, v_scale, bool(causal_top_left),
-                                         float(softmax_scale) if softmax_scale else 0.0, _MODES[mode], status, out,
-                                         lse)
+        # pools, scales, devices and metadata lengths are checked by the op (ValueError)
+        bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+        _op("paged_attention_out")(Q, K, V, _i32(q_len_per_seq), bt, _i32(num_blocks_per_seq),
+                                   _i32(kv_len_per_seq), k_scale, v_scale, bool(causal_top_left),
+                                   float(softmax_scale) if softmax_scale else 0.0, _MODES[mode], status, out, lse)
         if _CHECK and status is not None:
             _raise_status("paged_attention", status)
         return out, lse
+    for name, t in (("K", K), ("V", V), ("block_table", block_table), ("q_len_per_seq", q_len_per_seq),
+                    ("kv_len_per_seq", kv_len_per_seq), ("num_blocks_per_seq", num_blocks_per_seq)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, Q on {dev}")
     keep: list = []
     kc = kv_cache_desc(K, V, k_scale, v_scale)
     pg = paging_desc(block_table, num_blocks_per_seq, q_len_per_seq, kv_len_per_seq, keep)
@@ -343,7 +364,7 @@ def paged_attention_varlen(Q: torch.Tensor, cu_seqlens_q: torch.Tensor, K: torch
         check_cache(K, V, k_scale, v_scale)
         bt, nbk, ql, kl = _paging_tensors(block_table, num_blocks_per_seq, q_len, kv_len_per_seq)
         if T:
-            _torch_ops().paged_attention_varlen_out(Q, q_start, ql, int(max_q_len), K, V, bt, nbk, kl, k_scale,
+            _op("paged_attention_varlen_out")(Q, q_start, ql, int(max_q_len), K, V, bt, nbk, kl, k_scale,
                                                     v_scale, bool(causal_top_left),
                                                     float(softmax_scale) if softmax_scale else 0.0, status, out, lse)
         if _CHECK and status is not None:
@@ -442,9 +463,10 @@ def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor
         k_new = k_new.contiguous()
     if v_new.stride(2) != 1:
         v_new = v_new.contiguous()
-    check_cache(k_cache, v_cache, k_scale, v_scale)
-    if k_cache.dtype == torch.int8 and k_scale.dim() != 3:
+    if k_cache.dtype == torch.int8 and (k_scale is None or k_scale.dim() != 3):
         raise ValueError("quantise-on-write stores one scale per (token, head): scales must be [NB, BS, H]")
+    if BACKEND != "torch":
+        check_cache(k_cache, v_cache, k_scale, v_scale)  # the op checks them itself
     bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
     si, ps = _i32(seq_index), _i32(positions)
     if si.numel() != T or ps.numel() != T:
@@ -454,9 +476,8 @@ def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor
     if BACKEND == "torch":
         if bt.dim() != 2:
             raise ValueError("block_table must be 2-D [num_seqs, max_blocks]")
-        _torch_ops().write_kv(k_new, v_new, bt, si, ps, k_cache, v_cache,
-                              k_scale if k_cache.dtype == torch.int8 else None,
-                              v_scale if k_cache.dtype == torch.int8 else None, status)
+        _op("write_kv")(k_new, v_new, bt, si, ps, k_cache, v_cache, k_scale if k_cache.dtype == torch.int8 else None,
+                        v_scale if k_cache.dtype == torch.int8 else None, status)
         if _CHECK and status is not None:
             _raise_status("write_kv_cache", status)
         return
