@@ -1046,8 +1046,8 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
       if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
-    static const bool halves = std::getenv("PIE_B200_TC_HALVES") != nullptr;
-    if (!halves) {
+    static const bool quarters = std::getenv("PIE_B200_TC_QUARTERS") != nullptr;
+    if (quarters) {
       if (mma_bf16)
         return convert ? launch2(pa_prefill_tc2_kernel<true, true, true>)
                        : launch2(pa_prefill_tc2_kernel<true, false, true>);
