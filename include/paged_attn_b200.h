@@ -302,6 +302,40 @@ int kv_write_quant(const pa_kv_new_t* nw, const pa_kv_cache_t* kv, const pa_pagi
                    void* stream);
 
 /*
+ * K/V projection with the cache write in its epilogue: replaces
+ * transformer/model.py:75-82 (k = W_k(x), v = W_v(x), split into heads)
+ * followed by the cache write of :85-122.  For every token t and output n of
+ * W = [W_k; W_v] (nn.Linear's [out, in] layout, W_k's 2-D rows first):
+ *   out[t, n] = sum_c x[t, c] * W[n, c] + bias[n]   (fp32 accumulation)
+ * and output n = (kv, head h, d) goes to row (h, d) of token t's slot in the
+ * K (kv = 0) or V (kv = 1) pool, through block_table[seq_index[t]]
+ * [positions[t] / block_size] -- quantised with one scale per (token, head)
+ * exactly as kv_write_quant quantises its input rows for an INT8 pool, or
+ * rounded for an F16 / BF16 pool.  The projected rows never exist unpaged in
+ * device memory.  One launch on the tensor cores (tcgen05).
+ *   x         [num_tokens, d_model], PA_DTYPE_F16 or BF16, row stride x_stride
+ *   w         [2 * num_kv_heads * head_dim, d_model], same dtype, row stride w_stride
+ *   bias      fp32 [2 * num_kv_heads * head_dim], or NULL
+ * Limits: head_dim 128, d_model a positive multiple of 128, rows 16-byte
+ * aligned; an INT8 pool needs per-token scales.
+ */
+typedef struct {
+  const void* x;
+  const void* w;
+  const float* bias;
+  int64_t x_stride, w_stride;
+  int32_t dtype;
+  int32_t num_tokens;
+  int32_t d_model;
+  int32_t _reserved;
+  const int32_t* seq_index;
+  const int32_t* positions;
+} pa_kv_proj_t;
+
+int kv_project_write(const pa_kv_proj_t* pj, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                     void* stream);
+
+/*
  * Write of new K/V rows into an F16 / BF16 pool (round-to-nearest-even
  * conversion from the input dtype).  The pool fill of
  * tests/test_flash_attention.py:33-49 as a scatter through the block table.

@@ -828,6 +828,84 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
   return PA_OK;
 }
 
+// 2-D TMA map over a row-major [rows, cols] 16-bit matrix: box of 64 columns x 128 rows, 128-byte swizzle.
+static bool make_rows_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long row_stride) {
+  auto enc = encode_fn();
+  if (!enc || rows < 1 || cols < 64) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int kv_project_write(const pa_kv_proj_t* pj, const pa_kv_cache_t* kv, const pa_paging_t* pg, int32_t* status,
+                     void* stream) {
+  g_err[0] = 0;
+  if (!pj) return fail(PA_ERR_INVALID, "projection descriptor is NULL");
+  if (!pg) return fail(PA_ERR_INVALID, "paging descriptor is NULL");
+  int rc = check_cache(kv);
+  if (rc) return rc;
+  if (kv->dtype == PA_DTYPE_F32) return fail(PA_ERR_UNSUPPORTED, "kv_project_write writes int8, fp16 or bf16 pools");
+  if (kv->head_dim != 128) return fail(PA_ERR_UNSUPPORTED, "kv_project_write needs head_dim 128");
+  if (pj->dtype != PA_DTYPE_F16 && pj->dtype != PA_DTYPE_BF16)
+    return fail(PA_ERR_INVALID, "x / w must be fp16 or bf16");
+  if (pj->num_tokens < 0) return fail(PA_ERR_INVALID, "num_tokens < 0");
+  if (pj->d_model <= 0 || pj->d_model % 128) return fail(PA_ERR_UNSUPPORTED, "d_model must be a positive multiple of 128");
+  if (kv->dtype == PA_DTYPE_I8 && kv->ks_stride_slot == 0 && kv->block_size > 1)
+    return fail(PA_ERR_INVALID, "an int8 pool written per token needs per-token scales");
+  if (pj->num_tokens == 0) return PA_OK;
+  if (!pj->x || !pj->w || !pj->seq_index || !pj->positions || !pg->block_table)
+    return fail(PA_ERR_INVALID, "kv_project_write: NULL pointer");
+  if (!al(pj->x, 16) || !al(pj->w, 16) || !row_al(pj->x_stride, 2, 16) || !row_al(pj->w_stride, 2, 16) ||
+      pj->x_stride < pj->d_model || pj->w_stride < pj->d_model)
+    return fail(PA_ERR_INVALID, "x / w rows must be 16-byte aligned and hold d_model values");
+  if (pj->bias && !al(pj->bias, 4)) return fail(PA_ERR_INVALID, "bias misaligned");
+  pa::ProjParams p{};
+  p.k = kv->k;
+  p.v = kv->v;
+  p.k_sblk = kv->k_stride_block;
+  p.k_sslot = kv->k_stride_slot;
+  p.k_shead = kv->k_stride_head;
+  p.v_sblk = kv->v_stride_block;
+  p.v_sslot = kv->v_stride_slot;
+  p.v_shead = kv->v_stride_head;
+  p.cache_dtype = kv->dtype;
+  p.ks = kv->k_scale;
+  p.vs = kv->v_scale;
+  p.ks_sblk = kv->ks_stride_block;
+  p.ks_sslot = kv->ks_stride_slot;
+  p.ks_shead = kv->ks_stride_head;
+  p.vs_sblk = kv->vs_stride_block;
+  p.vs_sslot = kv->vs_stride_slot;
+  p.vs_shead = kv->vs_stride_head;
+  p.scale_f32 = kv->scale_dtype == PA_DTYPE_F32;
+  p.Hkv = kv->num_kv_heads;
+  p.D = kv->head_dim;
+  p.BS = kv->block_size;
+  p.log2BS = ilog2(kv->block_size);
+  p.NB = kv->num_blocks;
+  p.seq_idx = pj->seq_index;
+  p.pos = pj->positions;
+  p.T = pj->num_tokens;
+  p.bt = pg->block_table;
+  p.bt_ss = pg->bt_stride_seq;
+  p.bt_sc = pg->bt_stride_col;
+  p.bt_cols = pg->bt_cols;
+  p.num_seqs = pg->num_seqs;
+  p.status = status;
+  p.d_model = pj->d_model;
+  p.bias = pj->bias;
+  CUtensorMap xmap, wmap;
+  if (!make_rows_map(&xmap, pj->x, pj->num_tokens, pj->d_model, pj->x_stride) ||
+      !make_rows_map(&wmap, pj->w, 2LL * kv->num_kv_heads * kv->head_dim, pj->d_model, pj->w_stride))
+    return fail(PA_ERR_CUDA, "could not encode the TMA maps of x / w");
+  cudaError_t e = pa::launch_kv_project(p, xmap, wmap, pj->dtype == PA_DTYPE_BF16, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? PA_OK : cuda_fail(e, "kv_project_write launch");
+}
+
 static int block_pool_check(const pa_block_pool_t* pool, pa::PoolParams& p) {
   if (!pool) return fail(PA_ERR_INVALID, "block pool descriptor is NULL");
   if (pool->num_blocks < 0 || pool->max_seqs < 0 || pool->max_blocks_per_seq < 0)

@@ -277,6 +277,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
 // Fetch a TMA box into L2 only (no shared memory, no completion tracking).
 __device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int c0, int c1, int c2, int c3) {
   asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];\n" ::"l"(tmap), "r"(c0),
@@ -353,6 +361,30 @@ __device__ __forceinline__ void tc_mma_ss_k128(uint32_t d_tmem, uint64_t a0, uin
       " tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n}\n" ::"r"(d_tmem),
       "l"(a0), "l"(b0), "r"(idesc), "n"(AH), "n"(BH)
+      : "memory");
+}
+
+// tc_mma_ss_k128 onto an existing accumulator when `accumulate` is non-zero
+// (the first of the 8 steps adds to D instead of overwriting it).
+template <int AH, int BH>
+__device__ __forceinline__ void tc_mma_ss_k128_acc(uint32_t d_tmem, uint64_t a0, uint64_t b0, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p0, p1;\n .reg .b64 a1, a2, a3, a4, a5, a6, a7, b1, b2, b3, b4, b5, b6, b7;\n"
+      " setp.ne.b32 p0, %6, 0;\n setp.eq.b32 p1, %3, %3;\n"
+      " add.s64 a1, %1, 2;\n add.s64 a2, %1, 4;\n add.s64 a3, %1, 6;\n"
+      " add.s64 a4, %1, %4;\n add.s64 a5, a4, 2;\n add.s64 a6, a4, 4;\n add.s64 a7, a4, 6;\n"
+      " add.s64 b1, %2, 2;\n add.s64 b2, %2, 4;\n add.s64 b3, %2, 6;\n"
+      " add.s64 b4, %2, %5;\n add.s64 b5, b4, 2;\n add.s64 b6, b4, 4;\n add.s64 b7, b4, 6;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a4, b4, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a5, b5, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a6, b6, %3, p1;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], a7, b7, %3, p1;\n}\n" ::"r"(d_tmem),
+      "l"(a0), "l"(b0), "r"(idesc), "n"(AH), "n"(BH), "r"(accumulate)
       : "memory");
 }
 

@@ -145,6 +145,15 @@ cudaError_t launch_block_pool_apply(const PoolParams& p, const int* ops, int n_o
                                     cudaStream_t stream);
 cudaError_t launch_block_pool_step(const PoolParams& p, const StepParams& s, cudaStream_t stream);
 
+// K/V projection with the cache write in its epilogue (kv_project.cu): the
+// destination fields of WriteParams plus the projection's inner dimension and bias.
+struct ProjParams : WriteParams {
+  int d_model;
+  const float* bias;  // [2 * Hkv * D] or NULL
+};
+cudaError_t launch_kv_project(const ProjParams& p, const CUtensorMap& xmap, const CUtensorMap& wmap, int bf16,
+                              cudaStream_t stream);
+
 // Launchers implemented in the kernel translation units.
 cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream);
 // Decode: persistent grid size (CTAs) for a configuration on the current

@@ -6,6 +6,8 @@
 //   pie_b200::paged_attention_varlen(_out)  the same over packed query rows
 //   pie_b200::write_kv                      the quantise-on-write / copy of new
 //                                           K/V rows (transformer/model.py:85-122)
+//   pie_b200::project_write_kv              the K/V projection with that write in
+//                                           its epilogue (transformer/model.py:75-122)
 //
 // Each op reads pointers, sizes and element strides from its tensors, fills the
 // C structs of include/paged_attn_b200.h and calls the library on the current
@@ -333,6 +335,51 @@ void write_kv(const at::Tensor& k_new, const at::Tensor& v_new, const at::Tensor
   else check_rc(kv_write_copy(&nw, &kv, &pg, st, stream), "kv_write_copy");
 }
 
+void project_write_kv(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>& bias,
+                      const at::Tensor& block_table, const at::Tensor& seq_index, const at::Tensor& positions,
+                      at::Tensor& k_cache, at::Tensor& v_cache, const std::optional<at::Tensor>& k_scale,
+                      const std::optional<at::Tensor>& v_scale, const std::optional<at::Tensor>& status) {
+  TORCH_CHECK_VALUE(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && x.scalar_type() == w.scalar_type(),
+                    "pie_b200: x [T, d_model] and w [2 * Hkv * D, d_model] must share d_model and dtype");
+  TORCH_CHECK_VALUE(x.stride(1) == 1 && w.stride(1) == 1, "pie_b200: x / w need contiguous rows");
+  TORCH_CHECK_VALUE(w.size(0) == 2 * k_cache.size(2) * k_cache.size(3),
+                    "pie_b200: w must hold 2 * num_kv_heads * head_dim rows (W_k then W_v)");
+  check_device(k_cache, x, "x");
+  check_device(k_cache, w, "w");
+  check_device(k_cache, block_table, "block_table");
+  TORCH_CHECK_VALUE(block_table.scalar_type() == at::kInt && block_table.dim() == 2,
+                    "pie_b200: block_table must be int32 2-D");
+  const int64_t T = x.size(0);
+  check_i32(k_cache, seq_index, "seq_index", T);
+  check_i32(k_cache, positions, "positions", T);
+  if (bias.has_value()) {
+    check_device(k_cache, *bias, "bias");
+    TORCH_CHECK_VALUE(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == w.size(0),
+                      "pie_b200: bias must be a contiguous float32 vector of w's rows");
+  }
+  const c10::cuda::CUDAGuard guard(k_cache.device());
+  pa_kv_cache_t kv = kv_desc(k_cache, v_cache, k_scale, v_scale);
+  pa_paging_t pg{};
+  pg.block_table = static_cast<const int32_t*>(block_table.data_ptr());
+  pg.bt_stride_seq = block_table.stride(0);
+  pg.bt_stride_col = block_table.stride(1);
+  pg.bt_cols = static_cast<int32_t>(block_table.size(1));
+  pg.num_seqs = static_cast<int32_t>(block_table.size(0));
+  pa_kv_proj_t pj{};
+  pj.x = ptr(x);
+  pj.w = ptr(w);
+  pj.bias = bias.has_value() ? static_cast<const float*>(bias->data_ptr()) : nullptr;
+  pj.x_stride = x.stride(0);
+  pj.w_stride = w.stride(0);
+  pj.dtype = pa_dtype(x.scalar_type());
+  pj.num_tokens = static_cast<int32_t>(T);
+  pj.d_model = static_cast<int32_t>(x.size(1));
+  pj.seq_index = static_cast<const int32_t*>(seq_index.data_ptr());
+  pj.positions = static_cast<const int32_t*>(positions.data_ptr());
+  void* stream = c10::cuda::getCurrentCUDAStream(k_cache.device().index()).stream();
+  check_rc(kv_project_write(&pj, &kv, &pg, opt_ptr<int32_t>(status), stream), "kv_project_write");
+}
+
 // ---- shapes only (fake / meta tensors) ------------------------------------
 std::tuple<at::Tensor, at::Tensor> paged_attention_meta(const at::Tensor& Q, const at::Tensor&, const at::Tensor&,
                                                         const at::Tensor&, const at::Tensor&, const at::Tensor&,
@@ -368,6 +415,8 @@ TORCH_LIBRARY(pie_b200, m) {
         "bool causal_top_left, float softmax_scale, Tensor(s!)? status, Tensor(a!) out, Tensor(b!) lse) -> ()");
   m.def("write_kv(Tensor k_new, Tensor v_new, Tensor block_table, Tensor seq_index, Tensor positions, "
         "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor(c!)? k_scale, Tensor(d!)? v_scale, Tensor(s!)? status) -> ()");
+  m.def("project_write_kv(Tensor x, Tensor w, Tensor? bias, Tensor block_table, Tensor seq_index, Tensor positions, "
+        "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor(c!)? k_scale, Tensor(d!)? v_scale, Tensor(s!)? status) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(pie_b200, CUDA, m) {
@@ -376,6 +425,7 @@ TORCH_LIBRARY_IMPL(pie_b200, CUDA, m) {
   m.impl("paged_attention_varlen", &paged_attention_varlen);
   m.impl("paged_attention_varlen_out", &paged_attention_varlen_out);
   m.impl("write_kv", &write_kv);
+  m.impl("project_write_kv", &project_write_kv);
 }
 
 TORCH_LIBRARY_IMPL(pie_b200, Meta, m) {

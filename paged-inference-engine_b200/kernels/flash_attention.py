@@ -53,7 +53,8 @@ if _PKG_ROOT not in sys.path:
 
 from pie_b200 import ops as _ops  # noqa: E402
 
-__all__ = ["flash_attention_forward", "flash_attention_varlen", "FlashAttentionFunction", "write_kv_cache"]
+__all__ = ["flash_attention_forward", "flash_attention_varlen", "FlashAttentionFunction", "write_kv_cache",
+           "project_write_kv_cache"]
 
 
 def flash_attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_len_per_seq, block_table,
@@ -117,3 +118,16 @@ def write_kv_cache(k_new, v_new, block_table, seq_index, positions, k_cache, v_c
     """
     assert k_new.is_cuda and k_cache.is_cuda, "Not CUDA Tensors -_-"
     _ops.write_kv(k_new, v_new, block_table, seq_index, positions, k_cache, v_cache, k_scale, v_scale)
+
+
+def project_write_kv_cache(x, w_kv, bias, block_table, seq_index, positions, k_cache, v_cache, k_scale=None,
+                           v_scale=None):
+    """The K/V projection of transformer/model.py:75-82 with the cache write of :85-122 in its epilogue.
+
+    ``x`` [T, d_model] (float16 / bfloat16), ``w_kv`` = ``torch.cat([W_k.weight, W_v.weight])`` in the same
+    dtype, ``bias`` = ``torch.cat([W_k.bias, W_v.bias])`` (float32) or None.  One tensor-core launch computes
+    every token's K and V rows and writes them into the paged pool as ``write_kv_cache`` would (quantised
+    with one scale per (token, kv head) for INT8 pools); the projected rows never exist unpaged in memory.
+    """
+    assert x.is_cuda and k_cache.is_cuda, "Not CUDA Tensors -_-"
+    _ops.project_write_kv(x, w_kv, bias, block_table, seq_index, positions, k_cache, v_cache, k_scale, v_scale)

@@ -82,6 +82,15 @@ class PaKvNew(ctypes.Structure):
     ]
 
 
+class PaKvProj(ctypes.Structure):
+    """Mirror of pa_kv_proj_t."""
+
+    _fields_ = [
+        ("x", _vp), ("w", _vp), ("bias", _vp), ("x_stride", _i64), ("w_stride", _i64), ("dtype", _i32),
+        ("num_tokens", _i32), ("d_model", _i32), ("_reserved", _i32), ("seq_index", _vp), ("positions", _vp),
+    ]
+
+
 # name -> (restype, argtypes); every symbol include/paged_attn_b200.h declares.
 SIGNATURES = {
     "paged_attn_workspace_size": (ctypes.c_int, [ctypes.POINTER(PaAttnIO), ctypes.POINTER(PaKvCache),
@@ -114,6 +123,8 @@ SIGNATURES = {
                                       _vp, _vp]),
     "kv_write_copy": (ctypes.c_int, [ctypes.POINTER(PaKvNew), ctypes.POINTER(PaKvCache), ctypes.POINTER(PaPaging),
                                      _vp, _vp]),
+    "kv_project_write": (ctypes.c_int, [ctypes.POINTER(PaKvProj), ctypes.POINTER(PaKvCache),
+                                        ctypes.POINTER(PaPaging), _vp, _vp]),
     "block_pool_init": (ctypes.c_int, [_vp, _vp]),
     "block_pool_apply": (ctypes.c_int, [_vp, _vp, ctypes.c_int32, _vp, _vp]),
     "block_pool_step": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, _vp, ctypes.c_int64, ctypes.c_int32,

@@ -504,3 +504,56 @@ def write_kv(k_new: torch.Tensor, v_new: torch.Tensor, block_table: torch.Tensor
             _lib.check("kv_write_copy", lib.kv_write_copy(nw, kc, pg, _ptr(status), stream))
     if _CHECK and status is not None:
         _raise_status("write_kv_cache", status)
+
+
+def project_write_kv(x: torch.Tensor, w_kv: torch.Tensor, bias: Optional[torch.Tensor], block_table: torch.Tensor,
+                     seq_index: torch.Tensor, positions: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     k_scale: Optional[torch.Tensor] = None, v_scale: Optional[torch.Tensor] = None, *,
+                     status: Optional[torch.Tensor] = None) -> None:
+    """K/V projection of x [T, d_model] with the cache write in its epilogue (kv_project_write).
+
+    ``w_kv`` is [W_k; W_v] ([2 * Hkv * D, d_model], nn.Linear's weight layout)
+    and ``bias`` the matching float32 [2 * Hkv * D] (or None): token t's K
+    row of head h is ``x[t] @ W_k[h*D:(h+1)*D].T + b_k[h*D:(h+1)*D]``, written
+    at (seq_index[t], positions[t]) of the pool like ``write_kv`` writes it.
+    """
+    if x.dim() != 2 or w_kv.dim() != 2 or x.shape[1] != w_kv.shape[1]:
+        raise ValueError("x must be [T, d_model] and w_kv [2 * Hkv * D, d_model]")
+    if x.dtype not in (torch.float16, torch.bfloat16) or w_kv.dtype != x.dtype:
+        raise ValueError("x and w_kv must share a float16 or bfloat16 dtype")
+    if k_cache.dtype == torch.int8 and (k_scale is None or k_scale.dim() != 3):
+        raise ValueError("an int8 pool written per token needs per-token scales [NB, BS, H]")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if w_kv.stride(1) != 1:
+        w_kv = w_kv.contiguous()
+    dev = k_cache.device
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        bias = bias.to(torch.float32).contiguous()
+    bt = block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)
+    si, ps = _i32(seq_index), _i32(positions)
+    if status is None and _CHECK:
+        status = status_word(dev)
+    int8 = k_cache.dtype == torch.int8
+    if BACKEND == "torch":
+        _op("project_write_kv")(x, w_kv, bias, bt, si, ps, k_cache, v_cache, k_scale if int8 else None,
+                                v_scale if int8 else None, status)
+    else:
+        kc = kv_cache_desc(k_cache, v_cache, k_scale, v_scale)
+        pg = _lib.PaPaging()
+        pg.block_table = bt.data_ptr()
+        pg.bt_stride_seq, pg.bt_stride_col = bt.stride(0), bt.stride(1)
+        pg.bt_cols, pg.num_seqs = bt.shape[1], bt.shape[0]
+        pj = _lib.PaKvProj()
+        pj.x, pj.w = x.data_ptr(), w_kv.data_ptr()
+        pj.bias = None if bias is None else bias.data_ptr()
+        pj.x_stride, pj.w_stride = x.stride(0), w_kv.stride(0)
+        pj.dtype = _TORCH2PA[x.dtype]
+        pj.num_tokens, pj.d_model = x.shape[0], x.shape[1]
+        pj.seq_index, pj.positions = si.data_ptr(), ps.data_ptr()
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            _lib.check("kv_project_write", lib.kv_project_write(pj, kc, pg, _ptr(status),
+                                                                torch.cuda.current_stream(dev).cuda_stream))
+    if _CHECK and status is not None:
+        _raise_status("project_write_kv", status)

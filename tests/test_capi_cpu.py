@@ -41,7 +41,7 @@ def test_struct_layouts_match_header(tmp_path):
     from pie_b200.block_pool import PaBlockPool
 
     structs = {"pa_kv_cache_t": _lib.PaKvCache, "pa_paging_t": _lib.PaPaging, "pa_attn_io_t": _lib.PaAttnIO,
-               "pa_kv_new_t": _lib.PaKvNew, "pa_block_pool_t": PaBlockPool}
+               "pa_kv_new_t": _lib.PaKvNew, "pa_block_pool_t": PaBlockPool, "pa_kv_proj_t": _lib.PaKvProj}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "paged_attn_b200.h"', "int main(void) {"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
