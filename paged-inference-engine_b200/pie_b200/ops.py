@@ -523,6 +523,10 @@ def project_write_kv(x: torch.Tensor, w_kv: torch.Tensor, bias: Optional[torch.T
         raise ValueError("x and w_kv must share a float16 or bfloat16 dtype")
     if k_cache.dtype == torch.int8 and (k_scale is None or k_scale.dim() != 3):
         raise ValueError("an int8 pool written per token needs per-token scales [NB, BS, H]")
+    if w_kv.shape[0] != 2 * k_cache.shape[2] * k_cache.shape[3]:
+        raise ValueError(f"w_kv has {w_kv.shape[0]} rows; the pool needs 2 * {k_cache.shape[2]} * {k_cache.shape[3]}")
+    if seq_index.numel() != x.shape[0] or positions.numel() != x.shape[0]:
+        raise ValueError("seq_index / positions need one entry per token")
     if x.stride(1) != 1:
         x = x.contiguous()
     if w_kv.stride(1) != 1:

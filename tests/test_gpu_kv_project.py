@@ -5,7 +5,8 @@ same 16-bit inputs (x @ W^T + b, transformer/model.py:75-82) and written with
 the oracle's rule.  The GPU accumulates in float32 in another order, so a
 value can differ in its last bits: an INT8 code may differ by one where the
 quotient lies within 2e-3 of a rounding boundary (at most 0.1 % of the codes),
-a scale by one unit in the last place of its stored type; float16 pools hold
+an fp16 scale by one unit in its last place, an fp32 scale by 1e-5
+relative (the absmax's own accumulation-order error); float16 pools hold
 the rounded value (relative 2e-3).
 """
 import numpy as np
@@ -80,9 +81,13 @@ def test_projection_write_matches_float32(backend, dtype, pool, shape):
         if pool_t.dtype == torch.int8:
             q_ref, s_ref = orc.quantize_rows(want)  # fp32 rule of the reference
             s_got = sc_t.float().cpu().numpy()[blk, slot]
-            s_ref_st = s_ref.astype(np.float16 if sc_t.dtype == torch.float16 else np.float32)
-            ulp = np.spacing(np.abs(s_ref_st)).astype(np.float32)
-            assert (np.abs(s_got - s_ref_st.astype(np.float32)) <= ulp).all(), "scales"
+            if sc_t.dtype == torch.float16:  # one fp16 ulp
+                s_ref_st = s_ref.astype(np.float16)
+                tol = np.spacing(np.abs(s_ref_st)).astype(np.float32)
+            else:  # the row's absmax carries the accumulation-order error of a d_model-long dot product
+                s_ref_st = s_ref
+                tol = 1e-5 * np.abs(s_ref)
+            assert (np.abs(s_got - s_ref_st.astype(np.float32)) <= tol).all(), "scales"
             d = np.abs(got.astype(np.int32) - q_ref.astype(np.int32))
             assert d.max() <= 1, "INT8 codes differ by more than one"
             y = want / s_ref[..., None]
