@@ -508,7 +508,9 @@ class LongCtxWorkload(Workload):
         self.scaling = "strong"
         self.metric = ("long-context paged decode HBM GB/s, KV heads sharded over GPUs (INT8 KV, B=256, 64/8 heads, "
                        "ctx~U[8192,32768])")
-        self.kernel = "paged_attn_decode per GPU (split + merge, + NCCL all_gather)"
+        self.kernel = ("paged_attn_decode per GPU (split + merge" +
+                       (", output rows stored into peer buffers + barrier)" if exchange == "peer" and ws > 1
+                        else ", + NCCL all_gather)" if ws > 1 else ")"))
         self.dominant_name = "paged_attn_decode per GPU, local heads (split + merge, no collective)"
         self.launches = 2
         self.ws, self.rank = ws, rank
