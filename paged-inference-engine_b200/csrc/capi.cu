@@ -829,12 +829,13 @@ int paged_attn_decode_noalloc(const pa_attn_io_t* io, const pa_kv_cache_t* kv, c
 }
 
 // 2-D TMA map over a row-major [rows, cols] 16-bit matrix: box of 64 columns x 128 rows, 128-byte swizzle.
-static bool make_rows_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long row_stride) {
+static bool make_rows_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long row_stride,
+                          unsigned box_rows) {
   auto enc = encode_fn();
   if (!enc || rows < 1 || cols < 64) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
-  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t box[2] = {64, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -899,8 +900,9 @@ int kv_project_write(const pa_kv_proj_t* pj, const pa_kv_cache_t* kv, const pa_p
   p.d_model = pj->d_model;
   p.bias = pj->bias;
   CUtensorMap xmap, wmap;
-  if (!make_rows_map(&xmap, pj->x, pj->num_tokens, pj->d_model, pj->x_stride) ||
-      !make_rows_map(&wmap, pj->w, 2LL * kv->num_kv_heads * kv->head_dim, pj->d_model, pj->w_stride))
+  // boxes: 64 columns x 128 tokens of x, 64 columns x 256 outputs (two heads) of w
+  if (!make_rows_map(&xmap, pj->x, pj->num_tokens, pj->d_model, pj->x_stride, 128) ||
+      !make_rows_map(&wmap, pj->w, 2LL * kv->num_kv_heads * kv->head_dim, pj->d_model, pj->w_stride, 256))
     return fail(PA_ERR_CUDA, "could not encode the TMA maps of x / w");
   cudaError_t e = pa::launch_kv_project(p, xmap, wmap, pj->dtype == PA_DTYPE_BF16, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? PA_OK : cuda_fail(e, "kv_project_write launch");

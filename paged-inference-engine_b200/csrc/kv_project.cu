@@ -8,37 +8,47 @@
 //
 // Out[t, n] = sum_c X[t, c] * W[n, c] + bias[n] for the rows n of W = [W_k;
 // W_v] ([2 * Hkv * D, d_model], nn.Linear's [out, in] layout) and the tokens t
-// of X ([T, d_model]).  A CTA computes 128 tokens x 128 outputs -- one head of
-// K or of V -- on tcgen05:
-//   warp 4 (one lane)  TMA: X and W tiles of 128 rows x 128 columns (two
-//                      64-column SW128 boxes each) into a 3-stage ring;
-//   warp 5 (one lane)  8 x K16 MMAs per stage into a 128-column TMEM
-//                      accumulator (fp32), committing each stage free;
-//   warps 0-3          the epilogue: thread r owns token m0 + r (TMEM lane r):
-//                      bias, then for INT8 pools the row's absmax and the
-//                      reference's quantisation rule (quant.cuh), else a
-//                      rounded copy; the row goes to the token's slot of its
-//                      block (block_table[seq_index[t]][pos >> log2 BS]).
+// of X ([T, d_model]).  A tile is 128 tokens x 256 outputs -- two heads of K
+// and/or V (2 * Hkv heads in all, so Hkv tiles per 128 tokens).  The kernel is
+// persistent: one CTA per SM walks the tiles (outputs fastest, so the CTAs
+// resident at one time share their X rows in L2 and W stays L2-resident), with
+//   warp 8 (one lane)   TMA: X (128 x 64) and W (256 x 64) SW128 boxes into a
+//                       4-stage ring of 48 KB stages;
+//   warp 9 (one lane)   4 x (M128 N256 K16) MMAs per stage into one of two
+//                       256-column TMEM accumulators (fp32), committing each
+//                       stage free and each finished tile to the epilogue;
+//   warps 0-7           the epilogue of the previous tile while the next one
+//                       accumulates: warp w reads TMEM lanes 32 (w % 4).. of
+//                       head w / 4 of the tile, thread = one token: bias, then
+//                       for INT8 pools the row's absmax and the reference's
+//                       quantisation rule (quant.cuh), else a rounded copy;
+//                       the row goes to the token's slot of its block
+//                       (block_table[seq_index[t]][pos >> log2 BS]).
+// Roofline: tensor-bound, 2 * T * d_model * (2 * Hkv * D) FLOPs per launch;
+// the operand traffic per stage (48 KB for 128 x 256 x 64) is 96 B per MMA
+// cycle, inside the 128 B/clk shared-memory budget of the tensor core.
 #include "pa_common.cuh"
 #include "quant.cuh"
 
 namespace pa {
 namespace {
 
-constexpr int KP_BM = 128;             // tokens per CTA
-constexpr int KP_BN = 128;             // outputs per CTA (= head_dim)
-constexpr int KP_BK = 128;             // d_model columns per stage
-constexpr int KP_STAGES = 3;
-constexpr int KP_HALF = KP_BM * 128;   // one 64-column half of a 128-row tile: 16 KB
-constexpr int KP_TILE = 2 * KP_HALF;   // 32 KB
-constexpr int KP_A = 0;
-constexpr int KP_B = KP_STAGES * KP_TILE;
-constexpr int KP_BAR = 2 * KP_STAGES * KP_TILE;  // 192 KB
-constexpr int KP_BIAS = KP_BAR + 256;            // float[128]
-constexpr int KP_SMEM = KP_BIAS + 512 + 1024;    // + alignment slack
-constexpr int KP_THREADS = 192;
+constexpr int KP_BM = 128;                        // tokens per tile
+constexpr int KP_BN = 256;                        // outputs per tile (two heads)
+constexpr int KP_BK = 64;                         // d_model columns per stage (one SW128 atom row)
+constexpr int KP_STAGES = 4;
+constexpr int KP_A_BYTES = KP_BM * 128;           // 16 KB
+constexpr int KP_B_BYTES = KP_BN * 128;           // 32 KB
+constexpr int KP_STAGE = KP_A_BYTES + KP_B_BYTES;  // 48 KB
+constexpr int KP_BAR = KP_STAGES * KP_STAGE;      // 192 KB
+constexpr int KP_SMEM = KP_BAR + 256 + 1024;      // barriers + alignment slack
+constexpr int KP_EPI_WARPS = 8;
+constexpr int KP_PRODUCER = 8;
+constexpr int KP_MMA = 9;
+constexpr int KP_THREADS = 320;
+constexpr int KP_TMEM_COLS = 2 * KP_BN;           // two accumulators
 static_assert(KP_SMEM <= 227 * 1024, "shared memory per CTA");
-enum : int { P_FULL = 0, P_EMPTY = 3, P_DONE = 6, P_TMEMSLOT = 7 };
+enum : int { P_FULL = 0, P_EMPTY = 4, P_TFULL = 8, P_TEMPTY = 10, P_TMEMSLOT = 12 };
 
 // Bounded mbarrier wait; false (and a status bit) when it gives up.
 __device__ __forceinline__ bool kp_wait(int* status, uint32_t bar, uint32_t parity) {
@@ -46,6 +56,15 @@ __device__ __forceinline__ bool kp_wait(int* status, uint32_t bar, uint32_t pari
     if (mbar_try_wait(bar, parity)) return true;
   set_status(status, ST_WAIT_TIMEOUT);
   return false;
+}
+
+// The four K16 steps of one 64-column stage: descriptors advance 32 bytes
+// (2 in 16-byte units) per step inside the 128-byte swizzle atom.
+__device__ __forceinline__ void kp_mma_stage(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  tc_mma_ss(d, a, b, idesc, acc);
+  tc_mma_ss(d, a + 2, b + 2, idesc, 1u);
+  tc_mma_ss(d, a + 4, b + 4, idesc, 1u);
+  tc_mma_ss(d, a + 6, b + 6, idesc, 1u);
 }
 
 template <bool BF16>
@@ -62,8 +81,8 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int m0 = blockIdx.x * KP_BM;
-  const int n0 = blockIdx.y * KP_BN;  // rows of W: head blockIdx.y of K (< Hkv) or V
+  const int n_tiles = p.Hkv;  // 2 * Hkv heads, two per tile
+  const int tiles = n_tiles * ((p.T + KP_BM - 1) / KP_BM);
   const int nk = p.d_model / KP_BK;
 
   if (tid == 0) {
@@ -71,165 +90,207 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
       mbar_init(bar(P_FULL + s), 1);
       mbar_init(bar(P_EMPTY + s), 1);
     }
-    mbar_init(bar(P_DONE), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(P_TFULL + b), 1);
+      mbar_init(bar(P_TEMPTY + b), KP_EPI_WARPS);
+    }
     fence_mbar_init();
   }
-  if (warp == 5) {
-    tmem_alloc(bar(P_TMEMSLOT), 128);
+  if (warp == KP_MMA) {
+    tmem_alloc(bar(P_TMEMSLOT), KP_TMEM_COLS);
     tmem_relinquish();
   }
-  float* sbias = reinterpret_cast<float*>(sm + KP_BIAS);
-  if (tid < KP_BN) sbias[tid] = p.bias ? p.bias[n0 + tid] : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + KP_BAR + 8 * P_TMEMSLOT);
 
-  if (warp == 4) {
+  if (warp == KP_PRODUCER) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % KP_STAGES;
-        if (kb >= KP_STAGES) kp_wait(p.status, bar(P_EMPTY + s), ((kb / KP_STAGES) - 1) & 1);
-        mbar_arrive_expect_tx(bar(P_FULL + s), 2 * KP_TILE);
-        const uint32_t a = base + KP_A + s * KP_TILE;
-        const uint32_t b = base + KP_B + s * KP_TILE;
-        tma_load_2d(a, &xmap, bar(P_FULL + s), kb * KP_BK, m0);
-        tma_load_2d(a + KP_HALF, &xmap, bar(P_FULL + s), kb * KP_BK + 64, m0);
-        tma_load_2d(b, &wmap, bar(P_FULL + s), kb * KP_BK, n0);
-        tma_load_2d(b + KP_HALF, &wmap, bar(P_FULL + s), kb * KP_BK + 64, n0);
+      int it = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * KP_BM;
+        const int n0 = (tile % n_tiles) * KP_BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % KP_STAGES;
+          if (it >= KP_STAGES) kp_wait(p.status, bar(P_EMPTY + s), ((it / KP_STAGES) - 1) & 1);
+          mbar_arrive_expect_tx(bar(P_FULL + s), KP_STAGE);
+          const uint32_t a = base + s * KP_STAGE;
+          tma_load_2d(a, &xmap, bar(P_FULL + s), kb * KP_BK, m0);
+          tma_load_2d(a + KP_A_BYTES, &wmap, bar(P_FULL + s), kb * KP_BK, n0);
+        }
+      }
+      // every copy has landed before the CTA can exit (the MMA warp waits for
+      // them too; this covers a consumer that gave up on a bounded wait)
+      for (int s = 0; s < KP_STAGES && s < it; ++s) {
+        const int last = it - 1 - ((it - 1 - s) % KP_STAGES);
+        kp_wait(p.status, bar(P_FULL + s), (last / KP_STAGES) & 1);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == KP_MMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC = instr_desc_f16(BF16, false, false, KP_BM, KP_BN);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % KP_STAGES;
-        kp_wait(p.status, bar(P_FULL + s), (kb / KP_STAGES) & 1);
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+        const int b = lt & 1;
+        if (lt >= 2) kp_wait(p.status, bar(P_TEMPTY + b), ((lt >> 1) - 1) & 1);
         tc_fence_after();
-        tc_mma_ss_k128_acc<KP_HALF / 16, KP_HALF / 16>(tmem, smem_desc(base + KP_A + s * KP_TILE, 16, 1024),
-                                                       smem_desc(base + KP_B + s * KP_TILE, 16, 1024), IDESC,
-                                                       kb > 0 ? 1u : 0u);
-        tc_commit(bar(P_EMPTY + s));
+        const uint32_t d = tmem + b * KP_BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % KP_STAGES;
+          kp_wait(p.status, bar(P_FULL + s), (it / KP_STAGES) & 1);
+          tc_fence_after();
+          const uint32_t a = base + s * KP_STAGE;
+          kp_mma_stage(d, smem_desc(a, 16, 1024), smem_desc(a + KP_A_BYTES, 16, 1024), IDESC, kb > 0 ? 1u : 0u);
+          tc_commit(bar(P_EMPTY + s));
+        }
+        tc_commit(bar(P_TFULL + b));
       }
-      tc_commit(bar(P_DONE));
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 0-3)
-    const int r = tid;  // TMEM lane = token row
-    const int t = m0 + r;
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    kp_wait(p.status, bar(P_DONE), 0);
-    tc_fence_after();
-    // destination row of token t (range checks as the quantise-on-write kernel)
-    bool ok = t < p.T;
-    long long dst_k = 0, dst_s = 0;
-    if (ok) {
-      const int sq = p.seq_idx[t];
-      const int pos = p.pos[t];
-      if (sq < 0 || sq >= p.num_seqs) {
-        set_status(p.status, ST_BAD_SEQ_INDEX);
-        ok = false;
-      } else if (pos < 0 || (pos >> p.log2BS) >= p.bt_cols) {
-        set_status(p.status, ST_BAD_POSITION);
-        ok = false;
-      } else {
-        const int blk = p.bt[static_cast<long long>(sq) * p.bt_ss + static_cast<long long>(pos >> p.log2BS) * p.bt_sc];
-        if (blk < 0 || blk >= p.NB) {
-          set_status(p.status, ST_BAD_BLOCK_ID);
+    // ------------------------------------------------------------ epilogue (warps 0-7)
+    const int q = warp & 3;   // TMEM lane quarter
+    const int hf = warp >> 2; // head of the tile
+    const int r = q * 32 + lane;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+      const int b = lt & 1;
+      const int m0 = (tile / n_tiles) * KP_BM;
+      const int hh = 2 * (tile % n_tiles) + hf;  // head among [K heads | V heads]
+      const bool isv = hh >= p.Hkv;
+      const int h = isv ? hh - p.Hkv : hh;
+      const int t = m0 + r;
+      // destination row of token t (range checks as the quantise-on-write
+      // kernel), resolved while the tile accumulates; one of the two threads
+      // of a token reports
+      bool ok = t < p.T;
+      long long dst_k = 0, dst_s = 0;
+      if (ok) {
+        const int sq = p.seq_idx[t];
+        const int pos = p.pos[t];
+        if (sq < 0 || sq >= p.num_seqs) {
+          if (hf == 0) set_status(p.status, ST_BAD_SEQ_INDEX);
+          ok = false;
+        } else if (pos < 0 || (pos >> p.log2BS) >= p.bt_cols) {
+          if (hf == 0) set_status(p.status, ST_BAD_POSITION);
           ok = false;
         } else {
-          const int slot = pos & (p.BS - 1);
-          const int isv = blockIdx.y >= p.Hkv;
-          const int h = isv ? blockIdx.y - p.Hkv : blockIdx.y;
-          const long long b64 = blk;
-          dst_k = isv ? b64 * p.v_sblk + slot * p.v_sslot + h * p.v_shead : b64 * p.k_sblk + slot * p.k_sslot + h * p.k_shead;
-          dst_s = isv ? b64 * p.vs_sblk + slot * p.vs_sslot + h * p.vs_shead
-                      : b64 * p.ks_sblk + slot * p.ks_sslot + h * p.ks_shead;
+          const int blk =
+              p.bt[static_cast<long long>(sq) * p.bt_ss + static_cast<long long>(pos >> p.log2BS) * p.bt_sc];
+          if (blk < 0 || blk >= p.NB) {
+            if (hf == 0) set_status(p.status, ST_BAD_BLOCK_ID);
+            ok = false;
+          } else {
+            const int slot = pos & (p.BS - 1);
+            const long long b64 = blk;
+            dst_k = isv ? b64 * p.v_sblk + slot * p.v_sslot + h * p.v_shead
+                        : b64 * p.k_sblk + slot * p.k_sslot + h * p.k_shead;
+            dst_s = isv ? b64 * p.vs_sblk + slot * p.vs_sslot + h * p.vs_shead
+                        : b64 * p.ks_sblk + slot * p.ks_sslot + h * p.ks_shead;
+          }
         }
       }
-    }
-    const bool isv = blockIdx.y >= p.Hkv;
-    if (p.cache_dtype == PA_DTYPE_I8) {
-      // pass 1: the row's absmax (bias included); pass 2: quantise 32 values at a time
-      float amax = 0.f;
+      const float* bias = p.bias ? p.bias + hh * 128 : nullptr;  // head_dim 128 outputs per head
+      const uint32_t trow = tmem + b * KP_BN + hf * 128 + (static_cast<uint32_t>(q * 32) << 16);
+      kp_wait(p.status, bar(P_TFULL + b), (lt >> 1) & 1);
+      tc_fence_after();
+      if (p.cache_dtype == PA_DTYPE_I8) {
+        // pass 1: the row's absmax (bias included); pass 2: quantise 32 values at a time
+        float amax = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(trow + 32 * c, v);
-        tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(trow + 32 * c, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(__uint_as_float(v[i]) + sbias[32 * c + i]));
-      }
-      const float sc = amax == 0.f ? 1.0f : div127_rn(amax);
-      const float inv = rcp_approx(sc);
-      int8_t* row = static_cast<int8_t*>(isv ? p.v : p.k) + dst_k;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(trow + 32 * c, v);
-        tmem_wait_ld();
-        float f[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) + sbias[32 * c + i];
-        uint32_t w[8];
-        if (quant_row_fast<32>(f, inv, w)) quant_row_exact<32>(f, sc, w);
-        if (ok) {
-          uint4* d = reinterpret_cast<uint4*>(row + 32 * c);
-          d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          for (int i = 0; i < 32; ++i)
+            amax = fmaxf(amax, fabsf(__uint_as_float(v[i]) + (bias ? __ldg(bias + 32 * c + i) : 0.f)));
         }
-      }
-      if (ok) {
-        void* sp = isv ? p.vs : p.ks;
-        if (p.scale_f32) static_cast<float*>(sp)[dst_s] = sc;
-        else static_cast<__half*>(sp)[dst_s] = __float2half_rn(sc);
-      }
-    } else {
-      const bool bf = p.cache_dtype == PA_DTYPE_BF16;
-      uint16_t* row = static_cast<uint16_t*>(isv ? p.v : p.k) + dst_k;
+        const float sc = amax == 0.f ? 1.0f : div127_rn(amax);
+        const float inv = rcp_approx(sc);
+        int8_t* row = static_cast<int8_t*>(isv ? p.v : p.k) + dst_k;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(trow + 32 * c, v);
-        tmem_wait_ld();
-        uint32_t w[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(trow + 32 * c, v);
+          tmem_wait_ld();
+          float f[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float a = __uint_as_float(v[2 * i]) + sbias[32 * c + 2 * i];
-          const float b = __uint_as_float(v[2 * i + 1]) + sbias[32 * c + 2 * i + 1];
-          w[i] = bf ? pack2<true>(a, b) : pack2<false>(a, b);
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) + (bias ? __ldg(bias + 32 * c + i) : 0.f);
+          uint32_t w[8];
+          if (quant_row_fast<32>(f, inv, w)) quant_row_exact<32>(f, sc, w);
+          if (ok) {
+            uint4* d = reinterpret_cast<uint4*>(row + 32 * c);
+            d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          }
         }
         if (ok) {
-          uint4* d = reinterpret_cast<uint4*>(row + 32 * c);
+          void* sp = isv ? p.vs : p.ks;
+          if (p.scale_f32) static_cast<float*>(sp)[dst_s] = sc;
+          else static_cast<__half*>(sp)[dst_s] = __float2half_rn(sc);
+        }
+      } else {
+        const bool bf = p.cache_dtype == PA_DTYPE_BF16;
+        uint16_t* row = static_cast<uint16_t*>(isv ? p.v : p.k) + dst_k;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) d[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(trow + 32 * c, v);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float a = __uint_as_float(v[2 * i]) + (bias ? __ldg(bias + 32 * c + 2 * i) : 0.f);
+            const float e = __uint_as_float(v[2 * i + 1]) + (bias ? __ldg(bias + 32 * c + 2 * i + 1) : 0.f);
+            w[i] = bf ? pack2<true>(a, e) : pack2<false>(a, e);
+          }
+          if (ok) {
+            uint4* d = reinterpret_cast<uint4*>(row + 32 * c);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) d[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          }
         }
       }
+      // this warp's reads of the accumulator are done: hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_TEMPTY + b));
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == KP_MMA) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, KP_TMEM_COLS);
   }
+}
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (n[dev] == 0) {
+    int v = 0;
+    n[dev] = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0 ? v : 148;
+  }
+  return n[dev];
 }
 
 }  // namespace
 
-int kv_project_smem() { return KP_SMEM; }
-
 cudaError_t launch_kv_project(const ProjParams& p, const CUtensorMap& xmap, const CUtensorMap& wmap, int bf16,
                               cudaStream_t stream) {
   if (p.T == 0) return cudaSuccess;
-  const dim3 grid((p.T + KP_BM - 1) / KP_BM, 2 * p.Hkv);
+  const long long tiles = static_cast<long long>(p.Hkv) * ((p.T + KP_BM - 1) / KP_BM);
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
   auto go = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KP_SMEM);
     if (e != cudaSuccess) return e;
-    e = launch_pdl(kern, grid, dim3(KP_THREADS), KP_SMEM, stream, p, xmap, wmap);
+    e = launch_pdl(kern, dim3(grid), dim3(KP_THREADS), KP_SMEM, stream, p, xmap, wmap);
     return e != cudaSuccess ? e : cudaGetLastError();
   };
   return bf16 ? go(kv_project_kernel<true>) : go(kv_project_kernel<false>);

@@ -46,11 +46,22 @@ def _setup(seed, T_per_seq, d_model, Hkv, BS, dtype):
 @pytest.mark.parametrize("pool", ["i8_f16scale", "i8_f32scale", "f16"])
 @pytest.mark.parametrize("shape", [(256, 2, 16), (1024, 8, 16), (512, 4, 32)])
 def test_projection_write_matches_float32(backend, dtype, pool, shape):
+    _check_projection(backend, dtype, pool, shape, [130, 7, 163])
+
+
+@pytest.mark.parametrize("pool", ["i8_f16scale", "f16"])
+def test_projection_write_many_tiles_per_cta(pool):
+    """20100 tokens x 8 heads: ~1260 tiles, so every CTA of the persistent grid
+    walks several tiles and both TMEM accumulators take turns."""
+    _check_projection("torch", torch.bfloat16, pool, (512, 8, 16), [7000, 9000, 4100])
+
+
+def _check_projection(backend, dtype, pool, shape, t_per_seq):
     from pie_b200 import ops
     from pie_b200.workloads import empty_head_major_scales
 
     d_model, Hkv, BS = shape
-    x, w, bias, bt, seq, pos, ref, NB = _setup(11, [130, 7, 163], d_model, Hkv, BS, dtype)
+    x, w, bias, bt, seq, pos, ref, NB = _setup(11, t_per_seq, d_model, Hkv, BS, dtype)
     dev = torch.device("cuda")
     D = 128
     if pool.startswith("i8"):
