@@ -1,7 +1,8 @@
 """Benchmark of the B200 paged-attention hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload long_ctx_int8|decode_fp16|decode_int8|prefill_bf16]
+                    [--workload long_ctx_int8|decode_fp16|decode_int8|prefill_bf16|prefill_int8|
+                                project_write_int8]
                     [--exchange nccl|peer] [--no-extra] [--no-cpu-baseline]
 
 One step = one pass of the hot path over one batch of seeded synthetic input
@@ -24,9 +25,12 @@ with the reference's benchmark shapes (no public dataset is involved):
   prefill_int8  the same prefill over an INT8 pool (fp16 Q, quantise-on-write of
                 the new rows); the attention call dequantises the blocks it reads
                 once into fp16 scratch and runs the tcgen05 kernel.
+  project_write_int8  the K/V projection of the prefill_bf16 tokens (x [T, 4096]
+                bf16, W [2048, 4096]) with the INT8 cache write in its
+                epilogue, one launch.  Metric: TFLOP/s of the projection.
 
 On one GPU the line also carries, under ``workloads``, a full record (value,
-roofline, e2e, clocks, cpu_baseline) for each of the other four workloads,
+roofline, e2e, clocks, cpu_baseline) for each of the other five workloads,
 timed the same way in the same run.  ``roofline`` describes the dominant
 launches: the attention call alone (no write kernel, no collective) on the
 same inputs, timed by a second CUDA-event loop after the timed region; its
@@ -485,6 +489,95 @@ class PrefillWorkload(Workload):
         return f"{n} blocks of {self.ROWS} query rows drawn from the workload's sequences, {t:.1f} s"
 
 
+class ProjectWriteWorkload(Workload):
+    """project_write_int8: the K/V projection of a prefill batch with the INT8 cache write in its epilogue.
+
+    x [T, 4096] bf16 with T the prefill_bf16 tokens (B=8, L ~ U[1024, 4096]), W = [W_k; W_v]
+    [2 * 8 * 128, 4096] bf16, fp32 bias; every token's K and V rows are quantised (one fp16 scale per
+    token and head, head-major) into scattered blocks of 16 slots.  Metric: TFLOP/s of the projection.
+    """
+
+    ROWS = 64  # tokens per CPU unit
+
+    def __init__(self, seed: int, device, cpu_only: bool = False):
+        from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
+
+        self.name = "project_write_int8"
+        cfg = CONFIGS["prefill_bf16"]
+        gen = torch.Generator().manual_seed(seed)
+        L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
+        Hq, Hkv, D, BS = cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
+        dm = Hq * D
+        bt, nblk, NB = block_tables(gen, L, BS)
+        T = sum(L)
+        self.T, self.dm, self.Hkv, self.D, self.BS, self.NB = T, dm, Hkv, D, BS, NB
+        self.x = torch.randn(T, dm, generator=gen).to(torch.bfloat16)
+        self.w = (torch.randn(2 * Hkv * D, dm, generator=gen) / dm ** 0.5).to(torch.bfloat16)
+        self.b = torch.randn(2 * Hkv * D, generator=gen) * 0.1
+        self.seq = torch.cat([torch.full((l,), i, dtype=torch.int32) for i, l in enumerate(L)])
+        self.pos = torch.cat([torch.arange(l, dtype=torch.int32) for l in L])
+        self.bt = bt
+        self.work = 2.0 * T * dm * 2 * Hkv * D
+        self.dominant_work = self.work
+        self.info = {"T": T, "d_model": dm, "Hkv": Hkv, "D": D, "block_size": BS, "x_dtype": "bfloat16",
+                     "kv_dtype": "int8", "scales": "fp16 per (token, head), head-major"}
+        self.unit, self.scale, self.bound, self.dtype = "TFLOP/s", 1e-12, "tensor", "bf16"
+        self.metric = ("K/V projection with the INT8 paged-cache write in its epilogue, TFLOP/s "
+                       "(T = prefill_bf16 tokens, d_model 4096, 8 KV heads, D=128)")
+        self.kernel = "kv_project_write (kv_project_kernel)"
+        self.dominant_name = "kv_project_kernel"
+        self.launches = 1
+        if not cpu_only:
+            self._device(device)
+
+    def _device(self, device):
+        from kernels.flash_attention import project_write_kv_cache
+        from pie_b200.workloads import empty_head_major_scales
+
+        host = _pin(self.x, self.seq, self.pos, self.bt)
+        xd, seqd, posd, btd = [t.to(device) for t in host]
+        wd, bd = self.w.to(device), self.b.to(device)
+        KV = torch.empty(2, self.NB, self.BS, self.Hkv, self.D, dtype=torch.int8, device=device)
+        ks = empty_head_major_scales(self.NB, self.BS, self.Hkv, device=device)
+        vs = empty_head_major_scales(self.NB, self.BS, self.Hkv, device=device)
+        self.dev = dict(x=xd, w=wd, b=bd, KV=KV)
+
+        def step():
+            project_write_kv_cache(xd, wd, bd, btd, seqd, posd, KV[0], KV[1], ks, vs)
+        self.step = self.dominant = step
+
+        hKV = [torch.empty(KV.shape, dtype=torch.int8).pin_memory() for _ in range(2)]
+        pipe = PipelinedInputs(host, hKV, device)
+        self.h2d = pipe.nbytes
+        self.d2h = KV.numel()
+
+        def run(s, v):
+            x, seq, pos, bt = v
+            project_write_kv_cache(x, wd, bd, bt, seq, pos, KV[0], KV[1], ks, vs)
+            return KV
+
+        self.e2e_step = lambda: pipe.step(run)
+        self.e2e_start, self.e2e_end = pipe.start, pipe.end
+
+    def cpu_unit(self, i):
+        """The reference's path for 64 tokens: x @ W^T + b in float32 (transformer/model.py:75-82), then
+        the per-(token, head) quantisation of the cache write (:85-122, restated in the oracle)."""
+        from oracle import paged_attention as orc
+
+        if not hasattr(self, "_wf"):
+            self._wf = self.w.float()
+        n = (self.T + self.ROWS - 1) // self.ROWS
+        lo = (i * 7919 % n) * self.ROWS
+        xs = self.x[lo:lo + self.ROWS].float()
+        y = torch.addmm(self.b, xs, self._wf.T).view(-1, 2, self.Hkv, self.D).numpy()
+        orc.quantize_rows(y[:, 0])
+        orc.quantize_rows(y[:, 1])
+        return 2.0 * xs.shape[0] * self.dm * 2 * self.Hkv * self.D
+
+    def sample_desc(self, n, t):
+        return f"{n} blocks of {self.ROWS} tokens (float32 projection + quantisation), {t:.1f} s"
+
+
 class LongCtxWorkload(Workload):
     """long_ctx_int8: B=256, 64/8 heads, ctx ~ U[8192, 32768], INT8; KV heads sharded over ranks."""
 
@@ -583,6 +676,8 @@ def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False,
         return PrefillWorkload(1000 + rank, device, cpu_only, int8=name == "prefill_int8")
     if name == "long_ctx_int8":
         return LongCtxWorkload(ws, rank, device, cpu_only, exchange, batch)
+    if name == "project_write_int8":
+        return ProjectWriteWorkload(1000 + rank, device, cpu_only)
     return DecodeWorkload(name, 1000 + rank, device, cpu_only)
 
 
@@ -683,7 +778,7 @@ def measure(w: Workload, a, device, ws: int, rank: int, local: int, peaks: dict,
     return rec
 
 
-EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8")
+EXTRA_WORKLOADS = ("decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8", "project_write_int8")
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
@@ -715,6 +810,8 @@ def reference_kernel_leg(w: Workload, a, device) -> dict:
     exact (q_len = kv_len).  Reported against the workload's own algorithmic
     work: the same bytes or causal FLOPs as ``value``.
     """
+    if w.name == "project_write_int8":
+        return reference_projection_leg(w, a, device)
     try:
         import triton
 
@@ -769,6 +866,30 @@ def reference_kernel_leg(w: Workload, a, device) -> dict:
         return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
 
 
+def reference_projection_leg(w: Workload, a, device) -> dict:
+    """The reference's projection on this B200: two float32 nn.Linear calls (W_k, W_v) over the same
+    tokens (transformer/model.py:75-76, cuBLAS).  Its cache write that follows, a per-token Python loop
+    with host synchronisations (:85-122), is not timed, so this leg is faster than the reference's path."""
+    try:
+        import torch.nn.functional as F
+
+        d = w.dev
+        x = d["x"].float()
+        Wk, Wv = d["w"].float().chunk(2)
+        bk, bv = d["b"].chunk(2)
+
+        def ref_step():
+            F.linear(x, Wk, bk)
+            F.linear(x, Wv, bv)
+        ms = time_steps(ref_step, a.steps, a.warmup, device, 1) / a.steps
+        val = w.dominant_work / (ms * 1e-3) * w.scale
+        return {"impl": "reference projection: float32 nn.Linear for W_k and W_v (cuBLAS), cache write not timed",
+                "value": round(val, 3), "unit": w.unit, "us_per_call": round(ms * 1e3, 2),
+                "tf32": bool(torch.backends.cuda.matmul.allow_tf32), "ours_over_reference": None}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
 def rank_traffic(w: Workload, ws: int):
     """DRAM bytes of one dominant launch on one rank (a strong-scaled rank reads 1/ws of the pool)."""
     t = read_traffic(f"{w.name}_dominant_kernel")
@@ -784,7 +905,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="long_ctx_int8",
-                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8", "long_ctx_int8"])
+                    choices=["decode_fp16", "decode_int8", "prefill_bf16", "prefill_int8", "project_write_int8",
+                             "long_ctx_int8"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",

@@ -125,9 +125,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     pa_prefill_tc_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
   pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  const int mtile = gridDim.x - 1 - blockIdx.x;  // longest (causal) tiles first
-  const int hq = blockIdx.y;
-  const int b = blockIdx.z;
+  // grid (head, sequence, query tile), the query tile slowest and counted down:
+  // CTAs are dispatched in x, y, z order, so every sequence's and head's last
+  // (longest causal) tiles start first and the short ones fill the tail
+  const int mtile = gridDim.z - 1 - blockIdx.z;
+  const int hq = blockIdx.x;
+  const int b = blockIdx.y;
   const int qlen = tc_seq_qlen(p, b);
   const int m0 = mtile * TC_BM;
   if (m0 >= qlen) return;
@@ -500,11 +503,11 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     pa_prefill_tc2_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
   pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  const int mtile = gridDim.x - 1 - blockIdx.x;
+  const int mtile = gridDim.z - 1 - blockIdx.z;  // longest tiles first, as in pa_prefill_tc_kernel
   const int pairs = p.G >> 1;
-  const int kvh = blockIdx.y / pairs;
-  const int hq0 = kvh * p.G + 2 * (blockIdx.y - kvh * pairs);
-  const int b = blockIdx.z;
+  const int kvh = blockIdx.x / pairs;
+  const int hq0 = kvh * p.G + 2 * (blockIdx.x - kvh * pairs);
+  const int b = blockIdx.y;
   const int qlen = tc_seq_qlen(p, b);
   const int m0 = mtile * TC_BM;
   if (m0 >= qlen) return;
@@ -1038,7 +1041,7 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
   const bool mma_bf16 = kv_kind == KV_BF16;
   const bool convert = (p.q_bf16 != 0) != mma_bf16;
   if ((p.G & 1) == 0 && !std::getenv("PIE_B200_TC_SINGLE")) {
-    const dim3 grid2((p.maxq + TC_BM - 1) / TC_BM, p.Hkv * (p.G / 2), p.B);
+    const dim3 grid2(p.Hkv * (p.G / 2), p.B, (p.maxq + TC_BM - 1) / TC_BM);
     auto launch2 = [&](auto kern) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM);
       if (e != cudaSuccess) return e;
@@ -1060,7 +1063,7 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
     return convert ? launch2(pa_prefill_tc2_kernel<false, true, false>)
                    : launch2(pa_prefill_tc2_kernel<false, false, false>);
   }
-  const dim3 grid((p.maxq + TC_BM - 1) / TC_BM, p.Hq, p.B);
+  const dim3 grid(p.Hq, p.B, (p.maxq + TC_BM - 1) / TC_BM);
   auto launch = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, T1_SMEM);
     if (e != cudaSuccess) return e;
