@@ -269,7 +269,9 @@ __global__ void __launch_bounds__(KP_THREADS, 1)
   }
 }
 
-int sm_count() {
+}  // namespace
+
+int device_sm_count() {
   static int n[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
@@ -280,13 +282,11 @@ int sm_count() {
   return n[dev];
 }
 
-}  // namespace
-
 cudaError_t launch_kv_project(const ProjParams& p, const CUtensorMap& xmap, const CUtensorMap& wmap, int bf16,
                               cudaStream_t stream) {
   if (p.T == 0) return cudaSuccess;
   const long long tiles = static_cast<long long>(p.Hkv) * ((p.T + KP_BM - 1) / KP_BM);
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  const int grid = static_cast<int>(tiles < device_sm_count() ? tiles : device_sm_count());
   auto go = [&](auto kern) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, KP_SMEM);
     if (e != cudaSuccess) return e;

@@ -154,6 +154,9 @@ struct ProjParams : WriteParams {
 cudaError_t launch_kv_project(const ProjParams& p, const CUtensorMap& xmap, const CUtensorMap& wmap, int bf16,
                               cudaStream_t stream);
 
+// Streaming multiprocessors of the current device (cached per device).
+int device_sm_count();
+
 // Launchers implemented in the kernel translation units.
 cudaError_t launch_kv_write(const WriteParams& p, cudaStream_t stream);
 // Decode: persistent grid size (CTAs) for a configuration on the current

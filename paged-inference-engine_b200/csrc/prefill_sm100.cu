@@ -91,6 +91,14 @@ __device__ __forceinline__ void named_barrier_sync(int id, int n) {
 // running into its own limit.
 __device__ unsigned int g_tc_abort_gen = 0;
 
+// Work counters of the persistent paired-head prefill grid.  Slot
+// (launch generation & 255) holds [next item, CTAs finished]; the last CTA of
+// a launch zeroes its slot, so a slot is ready for the next launch (also for
+// a replay of a captured graph, which reuses its generation).  Two launches
+// in flight at the same time use different slots unless their generations
+// are 256 apart.
+__device__ unsigned int g_pf_sched[256][2];
+
 // Bounded mbarrier wait; false (and a status bit) on time-out or abort.  The
 // first poll is inlined: a wait on a phase that has already completed costs
 // ~55 cycles this way against ~240 through the out-of-line loop.
@@ -489,7 +497,8 @@ constexpr int P2_K = 2 * TILE_B;
 constexpr int P2_V = P2_K + P2_KS * TILE_B;
 constexpr int P2_BAR = P2_V + P2_VS * TILE_B;     // 224 KB
 enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, C_VEMPTY = 10, C_SFULL = 12,
-             C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18 };
+             C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18, C_QEMPTY = 19, C_IFULL = 20, C_IEMPTY = 22,
+             C_RING = 24 };  // C_RING: two 16-byte work-item slots, bytes 192..223 of the barrier area
 
 constexpr int P2_THREADS = 576;   // 16 softmax warps + producer + MMA
 constexpr int P2_PRODUCER = 16;
@@ -498,20 +507,11 @@ constexpr int P2_XCH = P2_BAR + 256;              // float [2 heads][128 rows]
 constexpr int P2_SMEM = P2_XCH + 1024 + 1024;      // + alignment slack
 static_assert(P2_SMEM <= 227 * 1024, "shared memory per CTA");
 
-template <bool MMA_BF16, bool Q_CONVERT, bool QUART>
+template <bool MMA_BF16, bool Q_CONVERT>
 __global__ void __launch_bounds__(P2_THREADS, 1)
     pa_prefill_tc2_kernel(const AttnParams p, const __grid_constant__ TcMaps maps) {
   pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  const int mtile = gridDim.z - 1 - blockIdx.z;  // longest tiles first, as in pa_prefill_tc_kernel
-  const int pairs = p.G >> 1;
-  const int kvh = blockIdx.x / pairs;
-  const int hq0 = kvh * p.G + 2 * (blockIdx.x - kvh * pairs);
-  const int b = blockIdx.y;
-  const int qlen = tc_seq_qlen(p, b);
-  const int m0 = mtile * TC_BM;
-  if (m0 >= qlen) return;
-
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sm = smem_raw + (base - raw);
@@ -521,14 +521,30 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  const int nkeys = tc_seq_keys(p, b, qlen);
-  const int off = p.top_left ? 0 : p.kvlen[b] - qlen;
-  const int kend = min(nkeys, off + m0 + TC_BM);
-  const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
+  // Persistent: a CTA runs work items (head pair, sequence, 128-row query
+  // tile) until none is left.  Item i = (z * B + b) * pairs_total + pair, with
+  // query tile MT - 1 - z: every sequence's longest (causal) tiles are handed
+  // out first; tiles past a sequence's rows are skipped by the producer.  The
+  // producer takes items from a launch-wide counter and passes each, with its
+  // sequence's lengths, through a two-slot ring (IFULL / IEMPTY); it loads
+  // the next item's Q as soon as the last Q*K^T of the current one has read Q
+  // (QEMPTY) and its K/V tiles as ring stages free up, and the MMA warp starts
+  // the next item's Q*K^T behind the current item's last P*V, so consecutive
+  // items overlap.  Every barrier counts phases across items: tile gt + j of
+  // the CTA uses ring stage (gt + j) % stages and phase (gt + j) / stages, and
+  // the Q barriers count items with keys (qi).
+  const int pairs = p.G >> 1;
+  const int P = p.Hkv * pairs;
+  const int MT = (p.maxq + TC_BM - 1) / TC_BM;
+  const int PB = P * p.B;
+  const unsigned total = static_cast<unsigned>(PB) * static_cast<unsigned>(MT);
+  unsigned int* sched = g_pf_sched[p.abort_gen & 255u];
+  volatile int* ring = reinterpret_cast<volatile int*>(sm + P2_BAR + 8 * C_RING);  // [2][item, qlen, nkeys, off]
 
   if (tid == 0) {
     mbar_init(bar(C_QFULL), 1);
     mbar_init(bar(C_QREADY), 512);
+    mbar_init(bar(C_QEMPTY), 1);
     for (int s = 0; s < P2_KS; ++s) {
       mbar_init(bar(C_KFULL + s), 1);
       mbar_init(bar(C_KEMPTY + s), 1);
@@ -539,8 +555,10 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(C_SFULL + x), 1);
-      mbar_init(bar(C_PFULL + x), QUART ? 512 : 256);
+      mbar_init(bar(C_PFULL + x), 256);
       mbar_init(bar(C_ODONE + x), 1);
+      mbar_init(bar(C_IFULL + x), 1);
+      mbar_init(bar(C_IEMPTY + x), 17);  // the MMA lane and one lane of each softmax warp
     }
     fence_mbar_init();
   }
@@ -553,276 +571,178 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + P2_BAR + 8 * C_TMEMSLOT);
 
+  // the item of ring slot `slot`, for the MMA and softmax roles
+  auto take_item = [&](int it, int& item, int& qlen, int& nkeys, int& off) {
+    const int slot = it & 1;
+    wait_or_flag(p, bar(C_IFULL + slot), (it >> 1) & 1);
+    item = ring[4 * slot];
+    qlen = ring[4 * slot + 1];
+    nkeys = ring[4 * slot + 2];
+    off = ring[4 * slot + 3];
+  };
+
   if (warp == P2_PRODUCER) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && nt > 0) {
-      mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
-      // Q tile: rows m0.. of sequence b (ragged rows: rows q_start[b] + m0.. of the packed Q; rows past
-      // its end read as zeros and rows of the next sequence are computed but never stored)
-      const int q_row0 = p.q_start ? p.q_start[b] + m0 : m0;
-      const int q_seq = p.q_start ? 0 : b;
+    int gt = 0, qi = 0;
+    for (int it = 0;; ++it) {
+      int item = -1, qlen = 0, nkeys = 0, off = 0;
+      if (lane == 0) {
+        for (;;) {
+          const unsigned i = atomicAdd(&sched[0], 1u);
+          if (i >= total) break;
+          const int zz = static_cast<int>(i / static_cast<unsigned>(PB));
+          const int bb = (static_cast<int>(i) - zz * PB) / P;
+          const int ql = tc_seq_qlen(p, bb);
+          if ((MT - 1 - zz) * TC_BM < ql) {
+            item = static_cast<int>(i);
+            qlen = ql;
+            nkeys = tc_seq_keys(p, bb, ql);
+            off = p.top_left ? 0 : p.kvlen[bb] - ql;
+            break;
+          }
+        }
+        const int slot = it & 1;
+        if (it >= 2) wait_or_flag(p, bar(C_IEMPTY + slot), ((it >> 1) - 1) & 1);
+        ring[4 * slot] = item;
+        ring[4 * slot + 1] = qlen;
+        ring[4 * slot + 2] = nkeys;
+        ring[4 * slot + 3] = off;
+        mbar_arrive(bar(C_IFULL + slot));  // release: the slot's words are visible to its waiters
+      }
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item < 0) break;
+      qlen = __shfl_sync(0xffffffffu, qlen, 0);
+      nkeys = __shfl_sync(0xffffffffu, nkeys, 0);
+      off = __shfl_sync(0xffffffffu, off, 0);
+      const int zi = item / PB;
+      const int b = (item - zi * PB) / P;
+      const int hp = item - zi * PB - b * P;
+      const int m0 = (MT - 1 - zi) * TC_BM;
+      const int kvh = hp / pairs;
+      const int hq0 = kvh * p.G + 2 * (hp - kvh * pairs);
+      const int kend = min(nkeys, off + m0 + TC_BM);
+      const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
+      if (nt > 0) {
+        if (lane == 0) {
+          if (qi > 0) wait_or_flag(p, bar(C_QEMPTY), (qi - 1) & 1);  // the last item's Q*K^T have read Q
+          mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
+          // Q tile: rows m0.. of sequence b (ragged rows: rows q_start[b] + m0.. of the packed Q; rows past
+          // its end read as zeros and rows of the next sequence are computed but never stored)
+          const int q_row0 = p.q_start ? p.q_start[b] + m0 : m0;
+          const int q_seq = p.q_start ? 0 : b;
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, q_row0, hq0 + x, q_seq);
-        tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, q_row0, hq0 + x, q_seq);
+          for (int x = 0; x < 2; ++x) {
+            tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, q_row0, hq0 + x, q_seq);
+            tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, q_row0, hq0 + x, q_seq);
+          }
+        }
+        const int boxs = p.BS < 16 ? p.BS : 16;
+        const int nbox = TC_BN / boxs;  // <= 16 (block_size >= 8)
+        const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
+        auto fetch = [&](int j) {
+          const int key = j * TC_BN + lane * boxs;
+          int blk = p.NB;  // out of range: TMA fills the box with zeros
+          if (lane < nbox && key < nkeys) {
+            const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
+            if (x >= 0 && x < p.NB) blk = x;
+            else set_status(p.status, ST_BAD_BLOCK_ID);
+          }
+          return blk;
+        };
+        int blk = fetch(0);
+        for (int j = 0; j < nt; ++j) {
+          const int blk_next = (j + 1 < nt) ? fetch(j + 1) : p.NB;
+          const int slot = (j * TC_BN + lane * boxs) & (p.BS - 1);
+          const uint32_t roff = static_cast<uint32_t>(lane * boxs * 128);
+          const int g = gt + j;
+          const int ks = g % P2_KS;
+          const int vs = g % P2_VS;
+          if (lane == 0) {
+            if (g >= P2_KS) wait_or_flag(p, bar(C_KEMPTY + ks), ((g / P2_KS) - 1) & 1);
+            mbar_arrive_expect_tx(bar(C_KFULL + ks), TILE_B);
+          }
+          __syncwarp();
+          if (lane < nbox) {
+            const uint32_t dst = base + P2_K + ks * TILE_B + roff;
+            tma_load_4d(dst, &maps.k, bar(C_KFULL + ks), 0, kvh, blk < p.NB ? slot : 0, blk);
+            tma_load_4d(dst + HALF_B, &maps.k, bar(C_KFULL + ks), 64, kvh, blk < p.NB ? slot : 0, blk);
+          }
+          if (lane == 0) {
+            if (g >= P2_VS) wait_or_flag(p, bar(C_VEMPTY + vs), ((g / P2_VS) - 1) & 1);
+            mbar_arrive_expect_tx(bar(C_VFULL + vs), TILE_B);
+          }
+          __syncwarp();
+          if (lane < nbox) {
+            const uint32_t dst = base + P2_V + vs * TILE_B + roff;
+            tma_load_4d(dst, &maps.v, bar(C_VFULL + vs), 0, kvh, blk < p.NB ? slot : 0, blk);
+            tma_load_4d(dst + HALF_B, &maps.v, bar(C_VFULL + vs), 64, kvh, blk < p.NB ? slot : 0, blk);
+          }
+          blk = blk_next;
+        }
       }
-    }
-    if (nt > 0) {
-      const int boxs = p.BS < 16 ? p.BS : 16;
-      const int nbox = TC_BN / boxs;  // <= 16 (block_size >= 8)
-      const int* bt_row = p.bt + static_cast<long long>(b) * p.bt_ss;
-      auto fetch = [&](int j) {
-        const int key = j * TC_BN + lane * boxs;
-        int blk = p.NB;  // out of range: TMA fills the box with zeros
-        if (lane < nbox && key < nkeys) {
-          const int x = __ldg(bt_row + static_cast<long long>(key >> p.log2BS) * p.bt_sc);
-          if (x >= 0 && x < p.NB) blk = x;
-          else set_status(p.status, ST_BAD_BLOCK_ID);
-        }
-        return blk;
-      };
-      int blk = fetch(0);
-      for (int j = 0; j < nt; ++j) {
-        const int blk_next = (j + 1 < nt) ? fetch(j + 1) : p.NB;
-        const int slot = (j * TC_BN + lane * boxs) & (p.BS - 1);
-        const uint32_t roff = static_cast<uint32_t>(lane * boxs * 128);
-        const int ks = j % P2_KS;
-        const int vs = j % P2_VS;
-        if (lane == 0) {
-          if (j >= P2_KS) wait_or_flag(p, bar(C_KEMPTY + ks), ((j / P2_KS) - 1) & 1);
-          mbar_arrive_expect_tx(bar(C_KFULL + ks), TILE_B);
-        }
-        __syncwarp();
-        if (lane < nbox) {
-          const uint32_t dst = base + P2_K + ks * TILE_B + roff;
-          tma_load_4d(dst, &maps.k, bar(C_KFULL + ks), 0, kvh, blk < p.NB ? slot : 0, blk);
-          tma_load_4d(dst + HALF_B, &maps.k, bar(C_KFULL + ks), 64, kvh, blk < p.NB ? slot : 0, blk);
-        }
-        if (lane == 0) {
-          if (j >= P2_VS) wait_or_flag(p, bar(C_VEMPTY + vs), ((j / P2_VS) - 1) & 1);
-          mbar_arrive_expect_tx(bar(C_VFULL + vs), TILE_B);
-        }
-        __syncwarp();
-        if (lane < nbox) {
-          const uint32_t dst = base + P2_V + vs * TILE_B + roff;
-          tma_load_4d(dst, &maps.v, bar(C_VFULL + vs), 0, kvh, blk < p.NB ? slot : 0, blk);
-          tma_load_4d(dst + HALF_B, &maps.v, bar(C_VFULL + vs), 64, kvh, blk < p.NB ? slot : 0, blk);
-        }
-        blk = blk_next;
-      }
+      gt += nt;
+      qi += nt > 0;
     }
   } else if (warp == P2_MMA) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && nt > 0) {
+    if (lane == 0) {
       constexpr uint32_t IDESC_QK = instr_desc_f16(MMA_BF16, false, false, TC_BM, TC_BN);
       constexpr uint32_t IDESC_PV = instr_desc_f16(MMA_BF16, false, true, TC_BM, TC_D);
+      int gt = 0, qi = 0;
+      // j: tile of the current item; stages and phases run on gt + j
       auto qk = [&](int x, int j) {
-        const uint32_t kb = base + P2_K + (j % P2_KS) * TILE_B;
+        const uint32_t kb = base + P2_K + ((gt + j) % P2_KS) * TILE_B;
         const uint32_t qb = base + (x ? P2_QB : P2_QA);
         tc_mma_ss_k128<HALF_B / 16, HALF_B / 16>(tmem + s_col(x), smem_desc(qb, 16, 1024), smem_desc(kb, 16, 1024),
                                                  IDESC_QK);
         tc_commit(bar(C_SFULL + x));
       };
       auto pv = [&](int x, int j) {
-        wait_or_flag(p, bar(C_PFULL + x), j & 1);
+        wait_or_flag(p, bar(C_PFULL + x), (gt + j) & 1);
         tc_fence_after();
-        const uint32_t vb = base + P2_V + (j % P2_VS) * TILE_B;
+        const uint32_t vb = base + P2_V + ((gt + j) % P2_VS) * TILE_B;
         tc_mma_ts_seq<TC_BN / 16>(tmem + O_COL + 128 * x, tmem + s_col(x), smem_desc(vb, HALF_B, 1024), IDESC_PV,
                                   j > 0 ? 1u : 0u);
         tc_commit(bar(C_ODONE + x));
       };
-      wait_or_flag(p, bar(C_QREADY), 0);
-      wait_or_flag(p, bar(C_KFULL), 0);
-      tc_fence_after();
-      qk(0, 0);
-      qk(1, 0);
-      tc_commit(bar(C_KEMPTY));
-      for (int j = 0; j < nt; ++j) {
-        wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
-        pv(0, j);
-        const bool more = j + 1 < nt;
-        if (more) {
-          wait_or_flag(p, bar(C_KFULL + (j + 1) % P2_KS), ((j + 1) / P2_KS) & 1);
-          tc_fence_after();
-          qk(0, j + 1);
-        }
-        pv(1, j);
-        tc_commit(bar(C_VEMPTY + j % P2_VS));
-        if (more) {
-          qk(1, j + 1);
-          tc_commit(bar(C_KEMPTY + (j + 1) % P2_KS));
-        }
-      }
-    }
-  } else if constexpr (QUART) {
-    // ------------------------------------------------------------ softmax (warps 0-15), one head at a time
-    // Warp w serves TMEM lanes 32 (w % 4) .. (rows) and the keys [32 qt, 32 qt + 32) of every tile,
-    // qt = w / 4, and does head a, then head b, of every tile: all 16 warps (four per sub-partition)
-    // work on one head while the tensor core runs the other head's P*V and next Q*K^T.  The four
-    // quarters of a row combine their maxima through shared memory (as fp16: every quarter rounds
-    // and compares the same values, so all use the same reference max; P and the row sum are
-    // relative to it, which the final division and the LSE undo).
-    const int lg = warp & 3;        // lane group: TMEM lanes / rows 32 lg ..
-    const int qt = warp >> 2;       // key quarter of every tile
-    const int r = tid & 127;        // query row within the tile = TMEM lane
-    const int row = m0 + r;
-    const int gbar = 1 + lg;        // named barrier of the lane group's four warps (128 threads)
-    const uint32_t trow = tmem + (static_cast<uint32_t>(lg * 32) << 16);
-    __half* xq = reinterpret_cast<__half*>(sm + P2_XCH);  // [4 quarters][128 rows]
-    if (nt > 0) {
-      wait_or_flag(p, bar(C_QFULL), 0);
-      if constexpr (Q_CONVERT) {
-        uint4* q4 = reinterpret_cast<uint4*>(sm + P2_QA);
-#pragma unroll 4
-        for (int i = tid; i < 2 * TILE_B / 16; i += 512) {
-          uint4 v = q4[i];
-          v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
-          v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
-          v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
-          v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
-          q4[i] = v;
-        }
-        fence_proxy_async_smem();
-      }
-      mbar_arrive(bar(C_QREADY));
-    }
-    const int lim = min(nkeys, off + row + 1);
-    float m_ref[2] = {-INFINITY, -INFINITY};
-    float l[2] = {0.f, 0.f};
-    const float c2 = p.scale_log2;
-    for (int j = 0; j < nt; ++j) {
-      const int k0 = j * TC_BN + 32 * qt;  // first key of this quarter
-      const bool need_mask = (k0 + 32 > off + m0 + 1) || (k0 + 32 > nkeys);
-#pragma unroll
-      for (int x = 0; x < 2; ++x) {
-        const uint32_t scol = s_col(x);
-        wait_or_flag(p, bar(C_SFULL + x), j & 1);
+      for (int it = 0; it <= static_cast<int>(total); ++it) {
+        int item, qlen, nkeys, off;
+        take_item(it, item, qlen, nkeys, off);
+        mbar_arrive(bar(C_IEMPTY + (it & 1)));
+        if (item < 0) break;
+        const int zi = item / PB;
+        const int m0 = (MT - 1 - zi) * TC_BM;
+        const int kend = min(nkeys, off + m0 + TC_BM);
+        const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
+        if (nt == 0) continue;
+        if constexpr (Q_CONVERT) wait_or_flag(p, bar(C_QREADY), qi & 1);
+        else wait_or_flag(p, bar(C_QFULL), qi & 1);
+        wait_or_flag(p, bar(C_KFULL + gt % P2_KS), (gt / P2_KS) & 1);
         tc_fence_after();
-        uint32_t rr[32];
-        tmem_ld32(trow + scol + 32 * qt, rr);
-        tmem_wait_ld();
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (need_mask) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float v = (k0 + i < lim) ? __uint_as_float(rr[i]) : -INFINITY;
-            rr[i] = __float_as_uint(v);
-            mx4[i & 3] = fmaxf(mx4[i & 3], v);
+        qk(0, 0);
+        qk(1, 0);
+        tc_commit(bar(C_KEMPTY + gt % P2_KS));
+        if (nt == 1) tc_commit(bar(C_QEMPTY));  // Q is free once these products are done
+        for (int j = 0; j < nt; ++j) {
+          const int g = gt + j;
+          wait_or_flag(p, bar(C_VFULL + g % P2_VS), (g / P2_VS) & 1);
+          pv(0, j);
+          const bool more = j + 1 < nt;
+          if (more) {
+            wait_or_flag(p, bar(C_KFULL + (g + 1) % P2_KS), ((g + 1) / P2_KS) & 1);
+            tc_fence_after();
+            qk(0, j + 1);
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(rr[i]), __uint_as_float(rr[i + 1]));
-        }
-        // the row's maximum over the four quarters (also orders every quarter's S load before any P store)
-        xq[qt * 128 + r] = __float2half_ru(fminf(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), 65504.f));
-        named_barrier_sync(gbar, 128);
-        const float mrow = fmaxf(fmaxf(__half2float(xq[r]), __half2float(xq[128 + r])),
-                                 fmaxf(__half2float(xq[256 + r]), __half2float(xq[384 + r])));
-        named_barrier_sync(gbar, 128);  // every quarter has read before the next head's post
-        const float mx = mrow * c2;
-        float alpha = 1.f;
-        bool resc = false;
-        if (mx > m_ref[x] + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
-          alpha = ex2(m_ref[x] - mx);
-          resc = j > 0;
-          m_ref[x] = mx;
-        }
-        const float neg_m = (m_ref[x] == -INFINITY) ? 0.f : -m_ref[x];
-        // P of keys [32 qt, 32 qt + 32) goes to TMEM columns [16 qt, 16 qt + 16) of S_x
-        uint64_t lsum2 = f2_pack(0.f, 0.f);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float p0, p1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
-                           f2_pack(neg_m, neg_m)),
-                    p0, p1);
-          p0 = ex2(p0);
-          p1 = ex2(p1);
-          if (need_mask) {
-            const int kk = k0 + 2 * i;
-            if (kk >= lim) p0 = 0.f;
-            if (kk + 1 >= lim) p1 = 0.f;
-          }
-          lsum2 = f2_add(lsum2, f2_pack(p0, p1));
-          pk[i] = pack2<MMA_BF16>(p0, p1);
-        }
-        tmem_st16(trow + scol + 16 * qt, pk);
-        {
-          float a0, a1;
-          f2_unpack(lsum2, a0, a1);
-          l[x] = l[x] * alpha + (a0 + a1);
-        }
-        // O holds P*V(<j) complete (S_x(j) ready implies P*V_x(j-1) done): rescale this quarter of the row
-        if (__any_sync(0xffffffffu, resc)) {
-          const float a = resc ? alpha : 1.f;
-          uint32_t oo[32];
-          tmem_ld32(trow + O_COL + 128 * x + 32 * qt, oo);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) oo[i] = __float_as_uint(__uint_as_float(oo[i]) * a);
-          tmem_st32(trow + O_COL + 128 * x + 32 * qt, oo);
-        }
-        tmem_wait_st();
-        const int kt = j * TC_BN;
-        if (x == 0 && nkeys - kt < TC_BN) {
-          // keys past the sequence: zero their V rows (head a's P*V runs first); this quarter
-          // zeroes 64 bytes of the row: half qt >> 1, bytes 64 (qt & 1) ..
-          wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
-          if (kt + r >= nkeys) {
-            unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + (qt >> 1) * HALF_B + r * 128 + 64 * (qt & 1);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
-          }
-          fence_proxy_async_smem();
-        }
-        tc_fence_before();
-        mbar_arrive(bar(C_PFULL + x));
-      }
-    }
-    // ---- epilogue: O / l, LSE (the row sum is the sum of the four quarters' sums) ------------
-    // The K ring is free once the last P*V of head a has completed (every Q*K^T was issued
-    // before it); the four quarters exchange their sums there.
-    float* lx = reinterpret_cast<float*>(sm + P2_K);  // [2 heads][4 quarters][128 rows]
-    if (nt > 0) {
-      wait_or_flag(p, bar(C_ODONE + 0), (nt - 1) & 1);
-      wait_or_flag(p, bar(C_ODONE + 1), (nt - 1) & 1);
-      tc_fence_after();
-    }
-#pragma unroll
-    for (int x = 0; x < 2; ++x) lx[(x * 4 + qt) * 128 + r] = l[x];
-    named_barrier_sync(gbar, 128);
-#pragma unroll
-    for (int x = 0; x < 2; ++x) {
-      const float lt = (lx[(x * 4 + 0) * 128 + r] + lx[(x * 4 + 1) * 128 + r]) +
-                       (lx[(x * 4 + 2) * 128 + r] + lx[(x * 4 + 3) * 128 + r]);
-      const int hq = hq0 + x;
-      const bool valid = row < qlen;
-      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh +
-                     static_cast<long long>(row) * p.o_sm + 32 * qt;
-      if (nt > 0) {
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        uint32_t oo[32];
-        tmem_ld32(trow + O_COL + 128 * x + 32 * qt, oo);
-        tmem_wait_ld();
-        if (valid) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_f16(__uint_as_float(oo[8 * v + 0]) * inv, __uint_as_float(oo[8 * v + 1]) * inv);
-            w.y = pack_f16(__uint_as_float(oo[8 * v + 2]) * inv, __uint_as_float(oo[8 * v + 3]) * inv);
-            w.z = pack_f16(__uint_as_float(oo[8 * v + 4]) * inv, __uint_as_float(oo[8 * v + 5]) * inv);
-            w.w = pack_f16(__uint_as_float(oo[8 * v + 6]) * inv, __uint_as_float(oo[8 * v + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + 8 * v) = w;
+          pv(1, j);
+          tc_commit(bar(C_VEMPTY + g % P2_VS));
+          if (more) {
+            qk(1, j + 1);
+            tc_commit(bar(C_KEMPTY + (g + 1) % P2_KS));
+            if (j + 2 == nt) tc_commit(bar(C_QEMPTY));
           }
         }
-      } else if (valid) {
-        for (int d = 0; d < 32; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
-      }
-      if (valid && p.lse && qt == 0) {
-        const float L = lt > 0.f ? (m_ref[x] + lg2(lt)) * 0.6931471805599453f : -INFINITY;
-        static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
-            __float2half_rn(L);
+        gt += nt;
+        ++qi;
       }
     }
   } else {
@@ -830,190 +750,233 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     const int x = (warp >> 2) & 1;  // 0: head a, 1: head b
     const int hf = warp >> 3;       // key half of every tile
     const int r = tid & 127;        // query row within the tile = TMEM lane
-    const int row = m0 + r;
     const int bar_id = 1 + x;       // named barrier of this head's 256 threads
     const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t scol = s_col(x);
     const uint32_t ocol = O_COL + 128 * x + 64 * hf;
     float* xch = reinterpret_cast<float*>(sm + P2_XCH) + x * 128 + r;
-    if (nt > 0) {
-      wait_or_flag(p, bar(C_QFULL), 0);
-      if constexpr (Q_CONVERT) {
-        uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
-#pragma unroll 4
-        for (int i = hf * 128 + r; i < TILE_B / 16; i += 256) {
-          uint4 v = q4[i];
-          v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
-          v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
-          v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
-          v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
-          q4[i] = v;
-        }
-        fence_proxy_async_smem();
-      }
-      mbar_arrive(bar(C_QREADY));
-    }
-    // Half 1 posts a value, half 0 combines it with its own and posts the
-    // result, half 1 reads it back: two barriers, one float per row and head.
-    auto combine = [&](float v, bool is_max) {
-      if (hf) {
-        *xch = v;
-        named_barrier_sync(bar_id, 256);
-        named_barrier_sync(bar_id, 256);
-        return *xch;
-      }
-      named_barrier_sync(bar_id, 256);
-      const float o = *xch;
-      const float t = is_max ? fmaxf(v, o) : v + o;
-      *xch = t;
-      named_barrier_sync(bar_id, 256);
-      return t;
+    // tiles of an item (0 for none or the end marker)
+    auto item_tiles = [&](int itm, int nk, int of) {
+      if (itm < 0) return 0;
+      const int ke = min(nk, of + (MT - 1 - itm / PB) * TC_BM + TC_BM);
+      return ke > 0 ? (ke + TC_BN - 1) / TC_BN : 0;
     };
-    const int lim = min(nkeys, off + row + 1);
-    float m_ref = -INFINITY;
-    float l = 0.f;
-    // The MMA warp issues Q*K^T(x, j+1) after P*V(x, j), and a tcgen05.commit
-    // arrives only once every earlier tcgen05 operation of its thread has
-    // completed: S(x, j) ready implies P*V(x, j-1) done.  O-done is therefore
-    // waited on once, for the last P*V, in the epilogue.
-    for (int j = 0; j < nt; ++j) {
-      wait_or_flag(p, bar(C_SFULL + x), j & 1);
-      tc_fence_after();
-      const int k0 = j * TC_BN + 64 * hf;  // first key of this half
-      const bool need_mask = (k0 + 64 > off + m0 + 1) || (k0 + 64 > nkeys);
-      uint32_t r0[32], r1[32];
-      tmem_ld32(trow + scol + 64 * hf, r0);
-      tmem_ld32(trow + scol + 64 * hf + 32, r1);
-      tmem_wait_ld();
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (need_mask) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v0 = (k0 + i < lim) ? __uint_as_float(r0[i]) : -INFINITY;
-          const float v1 = (k0 + 32 + i < lim) ? __uint_as_float(r1[i]) : -INFINITY;
-          r0[i] = __float_as_uint(v0);
-          r1[i] = __float_as_uint(v1);
-          mx4[i & 3] = fmax3f(mx4[i & 3], v0, v1);
+    // Q arrives in the other 16-bit type: the item's Q tile is converted in
+    // place, then released to the MMA warp (without conversion the MMA warp
+    // waits for the Q tile itself).  A next item's Q is converted before the
+    // current item's epilogue, so its first Q*K^T overlaps that epilogue.
+    auto convert_q = [&](int q_phase) {
+      wait_or_flag(p, bar(C_QFULL), q_phase & 1);
+      uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
+#pragma unroll 4
+      for (int i = hf * 128 + r; i < TILE_B / 16; i += 256) {
+        uint4 v = q4[i];
+        v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
+        v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
+        v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
+        v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
+        q4[i] = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(C_QREADY));
+    };
+    int gt = 0, qi = 0;
+    int item, qlen, nkeys, off;
+    take_item(0, item, qlen, nkeys, off);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(C_IEMPTY));
+    if (Q_CONVERT && item_tiles(item, nkeys, off) > 0) convert_q(0);
+    for (int it = 0; it <= static_cast<int>(total); ++it) {
+      if (item < 0) break;
+      const int zi = item / PB;
+      const int b = (item - zi * PB) / P;
+      const int hp = item - zi * PB - b * P;
+      const int m0 = (MT - 1 - zi) * TC_BM;
+      const int kvh = hp / pairs;
+      const int hq0 = kvh * p.G + 2 * (hp - kvh * pairs);
+      const int nt = item_tiles(item, nkeys, off);
+      const int row = m0 + r;
+      // Half 1 posts a value, half 0 combines it with its own and posts the
+      // result, half 1 reads it back: two barriers, one float per row and head.
+      auto combine = [&](float v, bool is_max) {
+        if (hf) {
+          *xch = v;
+          named_barrier_sync(bar_id, 256);
+          named_barrier_sync(bar_id, 256);
+          return *xch;
         }
-      } else {
+        named_barrier_sync(bar_id, 256);
+        const float o = *xch;
+        const float t = is_max ? fmaxf(v, o) : v + o;
+        *xch = t;
+        named_barrier_sync(bar_id, 256);
+        return t;
+      };
+      const int lim = min(nkeys, off + row + 1);
+      float m_ref = -INFINITY;
+      float l = 0.f;
+      // The MMA warp issues Q*K^T(x, j+1) after P*V(x, j), and a tcgen05.commit
+      // arrives only once every earlier tcgen05 operation of its thread has
+      // completed: S(x, j) ready implies P*V(x, j-1) done.  O-done is therefore
+      // waited on once, for the last P*V, in the epilogue.
+      for (int j = 0; j < nt; ++j) {
+        wait_or_flag(p, bar(C_SFULL + x), (gt + j) & 1);
+        tc_fence_after();
+        const int k0 = j * TC_BN + 64 * hf;  // first key of this half
+        const bool need_mask = (k0 + 64 > off + m0 + 1) || (k0 + 64 > nkeys);
+        uint32_t r0[32], r1[32];
+        tmem_ld32(trow + scol + 64 * hf, r0);
+        tmem_ld32(trow + scol + 64 * hf + 32, r1);
+        tmem_wait_ld();
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(r0[i]), __uint_as_float(r1[i]));
-      }
-      const float mx = combine(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), true) * p.scale_log2;
-      float alpha = 1.f;
-      bool resc = false;
-      if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
-        alpha = ex2(m_ref - mx);
-        // O holds P*V of earlier tiles once j > 0, whatever this half's own sum
-        // is: both halves decide alike from the shared maximum.
-        resc = j > 0;
-        m_ref = mx;
-      }
-      const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
-      const float c2 = p.scale_log2;
-      // P of keys [64 hf + 16 q, +16) goes to TMEM columns [32 hf + 8 q, +8) of S
-      uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int h = q >> 1;
-        const uint32_t* rr = (h ? r1 : r0) + 16 * (q & 1);
-        uint32_t pk[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float p0, p1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
-                           f2_pack(neg_m, neg_m)),
-                    p0, p1);
-          if (emu_pair(i)) {
-            exp2_fma_x2(p0, p1);
-          } else {
-            p0 = ex2(p0);
-            p1 = ex2(p1);
+          for (int i = 0; i < 32; ++i) {
+            const float v0 = (k0 + i < lim) ? __uint_as_float(r0[i]) : -INFINITY;
+            const float v1 = (k0 + 32 + i < lim) ? __uint_as_float(r1[i]) : -INFINITY;
+            r0[i] = __float_as_uint(v0);
+            r1[i] = __float_as_uint(v1);
+            mx4[i & 3] = fmax3f(mx4[i & 3], v0, v1);
           }
-          if (need_mask) {
-            const int kk = k0 + 16 * q + 2 * i;
-            if (kk >= lim) p0 = 0.f;
-            if (kk + 1 >= lim) p1 = 0.f;
-          }
-          lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
-          pk[i] = pack2<MMA_BF16>(p0, p1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx4[i & 3] = fmax3f(mx4[i & 3], __uint_as_float(r0[i]), __uint_as_float(r1[i]));
         }
-        tmem_st8(trow + scol + 32 * hf + 8 * q, pk);
+        const float mx = combine(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), true) * p.scale_log2;
+        float alpha = 1.f;
+        bool resc = false;
+        if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
+          alpha = ex2(m_ref - mx);
+          // O holds P*V of earlier tiles once j > 0, whatever this half's own sum
+          // is: both halves decide alike from the shared maximum.
+          resc = j > 0;
+          m_ref = mx;
+        }
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        const float c2 = p.scale_log2;
+        // P of keys [64 hf + 16 q, +16) goes to TMEM columns [32 hf + 8 q, +8) of S
+        uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int h = q >> 1;
+          const uint32_t* rr = (h ? r1 : r0) + 16 * (q & 1);
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float p0, p1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(rr[2 * i]), __uint_as_float(rr[2 * i + 1])), f2_pack(c2, c2),
+                             f2_pack(neg_m, neg_m)),
+                      p0, p1);
+            if (emu_pair(i)) {
+              exp2_fma_x2(p0, p1);
+            } else {
+              p0 = ex2(p0);
+              p1 = ex2(p1);
+            }
+            if (need_mask) {
+              const int kk = k0 + 16 * q + 2 * i;
+              if (kk >= lim) p0 = 0.f;
+              if (kk + 1 >= lim) p1 = 0.f;
+            }
+            lsum2[h] = f2_add(lsum2[h], f2_pack(p0, p1));
+            pk[i] = pack2<MMA_BF16>(p0, p1);
+          }
+          tmem_st8(trow + scol + 32 * hf + 8 * q, pk);
+        }
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(lsum2[0], a0, a1);
+          f2_unpack(lsum2[1], b0, b1);
+          l = l * alpha + ((a0 + a1) + (b0 + b1));
+        }
+        // Rescale this half's O columns after the logits are dead (fewer live
+        // registers); P*V(j) is issued only after PFULL, so O is still P*V(<j).
+        if (__any_sync(0xffffffffu, resc)) {  // O holds P*V(<j), complete (see above)
+          const float a = resc ? alpha : 1.f;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t rr[32];
+            tmem_ld32(trow + ocol + 32 * c, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
+            tmem_st32(trow + ocol + 32 * c, rr);
+          }
+        }
+        tmem_wait_st();
+        const int kt = j * TC_BN;
+        if (x == 0 && nkeys - kt < TC_BN) {
+          // keys past the sequence: zero their V rows (head a's P*V runs first;
+          // each half zeroes its 64-column half of the row)
+          wait_or_flag(p, bar(C_VFULL + (gt + j) % P2_VS), ((gt + j) / P2_VS) & 1);
+          if (kt + r >= nkeys) {
+            unsigned char* vrow = sm + P2_V + ((gt + j) % P2_VS) * TILE_B + hf * HALF_B + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        mbar_arrive(bar(C_PFULL + x));
       }
-      {
-        float a0, a1, b0, b1;
-        f2_unpack(lsum2[0], a0, a1);
-        f2_unpack(lsum2[1], b0, b1);
-        l = l * alpha + ((a0 + a1) + (b0 + b1));
-      }
-      // Rescale this half's O columns after the logits are dead (fewer live
-      // registers); P*V(j) is issued only after PFULL, so O is still P*V(<j).
-      if (__any_sync(0xffffffffu, resc)) {  // O holds P*V(<j), complete (see above)
-        const float a = resc ? alpha : 1.f;
+      // ---- the next item (its Q converted now), then this item's epilogue
+      int n_item, n_qlen, n_nkeys, n_off;
+      take_item(it + 1, n_item, n_qlen, n_nkeys, n_off);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_IEMPTY + ((it + 1) & 1)));
+      if (Q_CONVERT && item_tiles(n_item, n_nkeys, n_off) > 0) convert_q(qi + (nt > 0));
+      // ---- epilogue: O / l, LSE ---------------------------------------------
+      const float lt = combine(l, false);
+      const int hq = hq0 + x;
+      const bool valid = row < qlen;
+      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
+                     64 * hf;
+      if (nt > 0) {
+        wait_or_flag(p, bar(C_ODONE + x), (gt + nt - 1) & 1);  // the item's last P*V
+        tc_fence_after();
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t rr[32];
           tmem_ld32(trow + ocol + 32 * c, rr);
           tmem_wait_ld();
+          if (valid) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
-          tmem_st32(trow + ocol + 32 * c, rr);
-        }
-      }
-      tmem_wait_st();
-      const int kt = j * TC_BN;
-      if (x == 0 && nkeys - kt < TC_BN) {
-        // keys past the sequence: zero their V rows (head a's P*V runs first;
-        // each half zeroes its 64-column half of the row)
-        wait_or_flag(p, bar(C_VFULL + j % P2_VS), (j / P2_VS) & 1);
-        if (kt + r >= nkeys) {
-          unsigned char* vrow = sm + P2_V + (j % P2_VS) * TILE_B + hf * HALF_B + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
-        }
-        fence_proxy_async_smem();
-      }
-      tc_fence_before();
-      mbar_arrive(bar(C_PFULL + x));
-    }
-    // ---- epilogue: O / l, LSE ---------------------------------------------
-    const float lt = combine(l, false);
-    const int hq = hq0 + x;
-    const bool valid = row < qlen;
-    __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
-                   64 * hf;
-    if (nt > 0) {
-      wait_or_flag(p, bar(C_ODONE + x), (nt - 1) & 1);  // the last P*V (phase nt-1)
-      tc_fence_after();
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t rr[32];
-        tmem_ld32(trow + ocol + 32 * c, rr);
-        tmem_wait_ld();
-        if (valid) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
-            w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
-            w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
-            w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+              w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+              w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+              w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
+            }
           }
         }
+      } else if (valid) {
+        for (int d = 0; d < 64; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
       }
-    } else if (valid) {
-      for (int d = 0; d < 64; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
-    }
-    if (valid && p.lse && hf == 0) {
-      const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
-      static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
-          __float2half_rn(L);
+      if (valid && p.lse && hf == 0) {
+        const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
+        static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+            __float2half_rn(L);
+      }
+      gt += nt;
+      qi += nt > 0;
+      item = n_item;
+      qlen = n_qlen;
+      nkeys = n_nkeys;
+      off = n_off;
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&sched[1], 1u) == gridDim.x - 1) {  // the launch's last CTA: ready the slot for the next
+      atomicExch(&sched[0], 0u);
+      atomicExch(&sched[1], 0u);
+    }
+  }
   if (warp == P2_MMA) {
     __syncwarp();
     tc_fence_after();
@@ -1041,7 +1004,9 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
   const bool mma_bf16 = kv_kind == KV_BF16;
   const bool convert = (p.q_bf16 != 0) != mma_bf16;
   if ((p.G & 1) == 0 && !std::getenv("PIE_B200_TC_SINGLE")) {
-    const dim3 grid2(p.Hkv * (p.G / 2), p.B, (p.maxq + TC_BM - 1) / TC_BM);
+    const long long items = static_cast<long long>(p.Hkv) * (p.G / 2) * p.B * ((p.maxq + TC_BM - 1) / TC_BM);
+    if (items >= (1LL << 31)) return cudaErrorInvalidValue;
+    const dim3 grid2(static_cast<unsigned>(items < device_sm_count() ? items : device_sm_count()));
     auto launch2 = [&](auto kern) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P2_SMEM);
       if (e != cudaSuccess) return e;
@@ -1049,19 +1014,9 @@ cudaError_t launch_prefill_tc(const AttnParams& p_in, const CUtensorMap& kmap, c
       if (e != cudaSuccess) return e;
       return cudaGetLastError();
     };
-    static const bool quarters = std::getenv("PIE_B200_TC_QUARTERS") != nullptr;
-    if (quarters) {
-      if (mma_bf16)
-        return convert ? launch2(pa_prefill_tc2_kernel<true, true, true>)
-                       : launch2(pa_prefill_tc2_kernel<true, false, true>);
-      return convert ? launch2(pa_prefill_tc2_kernel<false, true, true>)
-                     : launch2(pa_prefill_tc2_kernel<false, false, true>);
-    }
     if (mma_bf16)
-      return convert ? launch2(pa_prefill_tc2_kernel<true, true, false>)
-                     : launch2(pa_prefill_tc2_kernel<true, false, false>);
-    return convert ? launch2(pa_prefill_tc2_kernel<false, true, false>)
-                   : launch2(pa_prefill_tc2_kernel<false, false, false>);
+      return convert ? launch2(pa_prefill_tc2_kernel<true, true>) : launch2(pa_prefill_tc2_kernel<true, false>);
+    return convert ? launch2(pa_prefill_tc2_kernel<false, true>) : launch2(pa_prefill_tc2_kernel<false, false>);
   }
   const dim3 grid(p.Hq, p.B, (p.maxq + TC_BM - 1) / TC_BM);
   auto launch = [&](auto kern) {
