@@ -500,9 +500,20 @@ enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, 
              C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18, C_QEMPTY = 19, C_IFULL = 20, C_IEMPTY = 22,
              C_RING = 24 };  // C_RING: two 16-byte work-item slots, bytes 192..223 of the barrier area
 
-constexpr int P2_THREADS = 576;   // 16 softmax warps + producer + MMA
-constexpr int P2_PRODUCER = 16;
-constexpr int P2_MMA = 17;
+// PA_PF_ROW1 = 0 (default): two softmax threads per query row, each taking
+// 64 keys of every tile (16 softmax warps, 96 registers a thread), the row
+// maxima and sums combined through shared memory.  1: one thread per row (8
+// softmax warps, 168 registers a thread).  Measured on B200 (bf16, 32/8
+// heads): 773 against 750 TFLOP/s on the 8-prompt L ~ U[1024, 4096] batch and
+// 1107 against 1034 on one 16K prompt, but 363 against 391 on 64 prompts of
+// 512 tokens, where one row per thread's shorter epilogue pays off.
+#ifndef PA_PF_ROW1
+#define PA_PF_ROW1 0
+#endif
+constexpr int P2_SOFTMAX_WARPS = PA_PF_ROW1 ? 8 : 16;
+constexpr int P2_THREADS = 32 * (P2_SOFTMAX_WARPS + 2);  // softmax warps + producer + MMA
+constexpr int P2_PRODUCER = P2_SOFTMAX_WARPS;
+constexpr int P2_MMA = P2_SOFTMAX_WARPS + 1;
 constexpr int P2_XCH = P2_BAR + 256;              // float [2 heads][128 rows]
 constexpr int P2_SMEM = P2_XCH + 1024 + 1024;      // + alignment slack
 static_assert(P2_SMEM <= 227 * 1024, "shared memory per CTA");
@@ -543,7 +554,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
 
   if (tid == 0) {
     mbar_init(bar(C_QFULL), 1);
-    mbar_init(bar(C_QREADY), 512);
+    mbar_init(bar(C_QREADY), 32 * P2_SOFTMAX_WARPS);
     mbar_init(bar(C_QEMPTY), 1);
     for (int s = 0; s < P2_KS; ++s) {
       mbar_init(bar(C_KFULL + s), 1);
@@ -555,10 +566,10 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(C_SFULL + x), 1);
-      mbar_init(bar(C_PFULL + x), 256);
+      mbar_init(bar(C_PFULL + x), 16 * P2_SOFTMAX_WARPS);  // the head's softmax threads
       mbar_init(bar(C_ODONE + x), 1);
       mbar_init(bar(C_IFULL + x), 1);
-      mbar_init(bar(C_IEMPTY + x), 17);  // the MMA lane and one lane of each softmax warp
+      mbar_init(bar(C_IEMPTY + x), 1 + P2_SOFTMAX_WARPS);  // the MMA lane and one lane of each softmax warp
     }
     fence_mbar_init();
   }
@@ -745,6 +756,223 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         ++qi;
       }
     }
+#if PA_PF_ROW1
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0-7), one row per thread
+    // Warp w serves TMEM lanes 32 (w % 4) .. of head w / 4: thread r owns query row r of its head and
+    // all 128 keys of every tile, so the row's maximum and sum never leave the thread.
+    const int x = warp >> 2;  // 0: head a, 1: head b
+    const int r = tid & 127;  // query row within the tile = TMEM lane
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t scol = s_col(x);
+    const uint32_t ocol = O_COL + 128 * x;
+    // tiles of an item (0 for none or the end marker)
+    auto item_tiles = [&](int itm, int nk, int of) {
+      if (itm < 0) return 0;
+      const int ke = min(nk, of + (MT - 1 - itm / PB) * TC_BM + TC_BM);
+      return ke > 0 ? (ke + TC_BN - 1) / TC_BN : 0;
+    };
+    // Q arrives in the other 16-bit type: the item's Q tile is converted in
+    // place, then released to the MMA warp (without conversion the MMA warp
+    // waits for the Q tile itself).  A next item's Q is converted before the
+    // current item's epilogue, so its first Q*K^T overlaps that epilogue.
+    auto convert_q = [&](int q_phase) {
+      wait_or_flag(p, bar(C_QFULL), q_phase & 1);
+      uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
+#pragma unroll 4
+      for (int i = r; i < TILE_B / 16; i += 128) {
+        uint4 v = q4[i];
+        v.x = cvt_pair<!MMA_BF16, MMA_BF16>(v.x);
+        v.y = cvt_pair<!MMA_BF16, MMA_BF16>(v.y);
+        v.z = cvt_pair<!MMA_BF16, MMA_BF16>(v.z);
+        v.w = cvt_pair<!MMA_BF16, MMA_BF16>(v.w);
+        q4[i] = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(C_QREADY));
+    };
+    int gt = 0, qi = 0;
+    int item, qlen, nkeys, off;
+    take_item(0, item, qlen, nkeys, off);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar(C_IEMPTY));
+    if (Q_CONVERT && item_tiles(item, nkeys, off) > 0) convert_q(0);
+    for (int it = 0; it <= static_cast<int>(total); ++it) {
+      if (item < 0) break;
+      const int zi = item / PB;
+      const int b = (item - zi * PB) / P;
+      const int hp = item - zi * PB - b * P;
+      const int m0 = (MT - 1 - zi) * TC_BM;
+      const int kvh = hp / pairs;
+      const int hq0 = kvh * p.G + 2 * (hp - kvh * pairs);
+      const int nt = item_tiles(item, nkeys, off);
+      const int row = m0 + r;
+      const int lim = min(nkeys, off + row + 1);
+      float m_ref = -INFINITY;
+      float l = 0.f;
+      // The MMA warp issues Q*K^T(x, j+1) after P*V(x, j), and a tcgen05.commit
+      // arrives only once every earlier tcgen05 operation of its thread has
+      // completed: S(x, j) ready implies P*V(x, j-1) done.  O-done is therefore
+      // waited on once, for the last P*V, in the epilogue.
+      for (int j = 0; j < nt; ++j) {
+        wait_or_flag(p, bar(C_SFULL + x), (gt + j) & 1);
+        tc_fence_after();
+        const int k0 = j * TC_BN;
+        const bool need_mask = (k0 + TC_BN > off + m0 + 1) || (k0 + TC_BN > nkeys);
+        uint32_t s0[32], s1[32], s2[32], s3[32];
+        tmem_ld32(trow + scol, s0);
+        tmem_ld32(trow + scol + 32, s1);
+        tmem_ld32(trow + scol + 64, s2);
+        tmem_ld32(trow + scol + 96, s3);
+        tmem_wait_ld();
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float v0 = (k0 + i < lim) ? __uint_as_float(s0[i]) : -INFINITY;
+            const float v1 = (k0 + 32 + i < lim) ? __uint_as_float(s1[i]) : -INFINITY;
+            const float v2 = (k0 + 64 + i < lim) ? __uint_as_float(s2[i]) : -INFINITY;
+            const float v3 = (k0 + 96 + i < lim) ? __uint_as_float(s3[i]) : -INFINITY;
+            s0[i] = __float_as_uint(v0);
+            s1[i] = __float_as_uint(v1);
+            s2[i] = __float_as_uint(v2);
+            s3[i] = __float_as_uint(v3);
+            mx4[i & 3] = fmax3f(mx4[i & 3], fmax3f(v0, v1, v2), v3);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            mx4[i & 3] = fmax3f(mx4[i & 3], fmax3f(__uint_as_float(s0[i]), __uint_as_float(s1[i]), __uint_as_float(s2[i])),
+                                __uint_as_float(s3[i]));
+        }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+        float alpha = 1.f;
+        bool resc = false;
+        if (mx > m_ref + RESCALE_THRESHOLD) {  // also the first finite max (m_ref = -inf)
+          alpha = ex2(m_ref - mx);
+          resc = j > 0;  // O holds P*V of earlier tiles once j > 0
+          m_ref = mx;
+        }
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        const float c2 = p.scale_log2;
+        // P of keys [16 q, 16 q + 16) goes to TMEM columns [8 q, 8 q + 8) of S
+        uint64_t lsum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+        auto exp_chunk = [&](const uint32_t (&rv)[32], int kc) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float p0, p1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(rv[16 * q + 2 * i]), __uint_as_float(rv[16 * q + 2 * i + 1])),
+                               f2_pack(c2, c2), f2_pack(neg_m, neg_m)),
+                        p0, p1);
+              if (emu_pair(i)) {
+                exp2_fma_x2(p0, p1);
+              } else {
+                p0 = ex2(p0);
+                p1 = ex2(p1);
+              }
+              if (need_mask) {
+                const int kk = k0 + kc + 16 * q + 2 * i;
+                if (kk >= lim) p0 = 0.f;
+                if (kk + 1 >= lim) p1 = 0.f;
+              }
+              lsum2[q] = f2_add(lsum2[q], f2_pack(p0, p1));
+              pk[i] = pack2<MMA_BF16>(p0, p1);
+            }
+            tmem_st8(trow + scol + (kc >> 1) + 8 * q, pk);
+          }
+        };
+        exp_chunk(s0, 0);
+        exp_chunk(s1, 32);
+        exp_chunk(s2, 64);
+        exp_chunk(s3, 96);
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(lsum2[0], a0, a1);
+          f2_unpack(lsum2[1], b0, b1);
+          l = l * alpha + ((a0 + a1) + (b0 + b1));
+        }
+        // Rescale the O row after the logits are dead (fewer live registers);
+        // P*V(j) is issued only after PFULL, so O is still P*V(<j).
+        if (__any_sync(0xffffffffu, resc)) {
+          const float a = resc ? alpha : 1.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t rr[32];
+            tmem_ld32(trow + ocol + 32 * c, rr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * a);
+            tmem_st32(trow + ocol + 32 * c, rr);
+          }
+        }
+        tmem_wait_st();
+        const int kt = j * TC_BN;
+        if (x == 0 && nkeys - kt < TC_BN) {
+          // keys past the sequence: zero their V rows (head a's P*V runs first)
+          wait_or_flag(p, bar(C_VFULL + (gt + j) % P2_VS), ((gt + j) / P2_VS) & 1);
+          if (kt + r >= nkeys) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              unsigned char* vrow = sm + P2_V + ((gt + j) % P2_VS) * TILE_B + h * HALF_B + r * 128;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(vrow + 16 * c) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        mbar_arrive(bar(C_PFULL + x));
+      }
+      // ---- the next item (its Q converted now), then this item's epilogue
+      int n_item, n_qlen, n_nkeys, n_off;
+      take_item(it + 1, n_item, n_qlen, n_nkeys, n_off);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(C_IEMPTY + ((it + 1) & 1)));
+      if (Q_CONVERT && item_tiles(n_item, n_nkeys, n_off) > 0) convert_q(qi + (nt > 0));
+      // ---- epilogue: O / l, LSE ---------------------------------------------
+      const int hq = hq0 + x;
+      const bool valid = row < qlen;
+      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm;
+      if (nt > 0) {
+        wait_or_flag(p, bar(C_ODONE + x), (gt + nt - 1) & 1);  // the item's last P*V
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(trow + ocol + 32 * c, rr);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+              w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+              w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+              w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
+              *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
+            }
+          }
+        }
+      } else if (valid) {
+        for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+      }
+      if (valid && p.lse) {
+        const float L = l > 0.f ? (m_ref + lg2(l)) * 0.6931471805599453f : -INFINITY;
+        static_cast<__half*>(p.lse)[l_seq_base(p, b) + hq * p.l_sh + static_cast<long long>(row) * p.l_sm] =
+            __float2half_rn(L);
+      }
+      gt += nt;
+      qi += nt > 0;
+      item = n_item;
+      qlen = n_qlen;
+      nkeys = n_nkeys;
+      off = n_off;
+    }
+#else
   } else {
     // ------------------------------------------------------------ softmax (warps 0-15)
     const int x = (warp >> 2) & 1;  // 0: head a, 1: head b
@@ -967,6 +1195,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       nkeys = n_nkeys;
       off = n_off;
     }
+#endif
   }
   tc_fence_before();
   __syncthreads();
