@@ -99,6 +99,31 @@ __device__ unsigned int g_tc_abort_gen = 0;
 // are 256 apart.
 __device__ unsigned int g_pf_sched[256][2];
 
+// 8 x 8 transpose of 16-byte pieces across the eight lanes of a group (lane
+// index i = lane & 7): on return lane i holds piece i of lanes 0..7's rows.
+// Three butterfly stages; in stage m a lane swaps, with lane i ^ m, the four
+// pieces whose index differs from i in bit m (selects on compile-time
+// indices, 16 shuffles a stage).
+__device__ __forceinline__ void transpose8_u4(uint4 (&v)[8], int i) {
+#pragma unroll
+  for (int m = 1; m < 8; m <<= 1) {
+    const bool hi = (i & m) != 0;
+#pragma unroll
+    for (int j0 = 0; j0 < 8; ++j0) {
+      if (j0 & m) continue;
+      const int j1 = j0 | m;
+      const uint4 t = hi ? v[j0] : v[j1];
+      uint4 u;
+      u.x = __shfl_xor_sync(0xffffffffu, t.x, m);
+      u.y = __shfl_xor_sync(0xffffffffu, t.y, m);
+      u.z = __shfl_xor_sync(0xffffffffu, t.z, m);
+      u.w = __shfl_xor_sync(0xffffffffu, t.w, m);
+      if (hi) v[j0] = u;
+      else v[j1] = u;
+    }
+  }
+}
+
 // Bounded mbarrier wait; false (and a status bit) on time-out or abort.  The
 // first poll is inlined: a wait on a phase that has already completed costs
 // ~55 cycles this way against ~240 through the out-of-line loop.
@@ -1157,8 +1182,8 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       const float lt = combine(l, false);
       const int hq = hq0 + x;
       const bool valid = row < qlen;
-      __half* orow = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + static_cast<long long>(row) * p.o_sm +
-                     64 * hf;
+      // this thread's 64 output columns of its row, as eight 16-byte pieces
+      uint4 ov[8];
       if (nt > 0) {
         wait_or_flag(p, bar(C_ODONE + x), (gt + nt - 1) & 1);  // the item's last P*V
         tc_fence_after();
@@ -1168,20 +1193,32 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
           uint32_t rr[32];
           tmem_ld32(trow + ocol + 32 * c, rr);
           tmem_wait_ld();
-          if (valid) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
-              w.y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
-              w.z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
-              w.w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
-              *reinterpret_cast<uint4*>(orow + 32 * c + 8 * v) = w;
-            }
+          for (int v = 0; v < 4; ++v) {
+            ov[4 * c + v].x = pack_f16(__uint_as_float(rr[8 * v + 0]) * inv, __uint_as_float(rr[8 * v + 1]) * inv);
+            ov[4 * c + v].y = pack_f16(__uint_as_float(rr[8 * v + 2]) * inv, __uint_as_float(rr[8 * v + 3]) * inv);
+            ov[4 * c + v].z = pack_f16(__uint_as_float(rr[8 * v + 4]) * inv, __uint_as_float(rr[8 * v + 5]) * inv);
+            ov[4 * c + v].w = pack_f16(__uint_as_float(rr[8 * v + 6]) * inv, __uint_as_float(rr[8 * v + 7]) * inv);
           }
         }
-      } else if (valid) {
-        for (int d = 0; d < 64; d += 8) *reinterpret_cast<uint4*>(orow + d) = make_uint4(0, 0, 0, 0);
+      } else {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) ov[v] = make_uint4(0, 0, 0, 0);
+      }
+      // Coalesced stores: the eight lanes of a group (rows 8 g .. 8 g + 7 of
+      // the warp) transpose their 8 x 8 pieces, so that store k writes row
+      // 8 g + k as 128 contiguous bytes, four rows per warp instruction
+      // instead of 32 scattered 16-byte pieces.
+      transpose8_u4(ov, lane & 7);
+      {
+        const int gi = lane & 7;
+        const int r0 = (warp & 3) * 32 + (lane & ~7);  // first row of this lane's group
+        __half* obase = static_cast<__half*>(p.o) + o_seq_base(p, b) + hq * p.o_sh + 64 * hf + 8 * gi;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int rw = m0 + r0 + kk;
+          if (rw < qlen) *reinterpret_cast<uint4*>(obase + static_cast<long long>(rw) * p.o_sm) = ov[kk];
+        }
       }
       if (valid && p.lse && hf == 0) {
         const float L = lt > 0.f ? (m_ref + lg2(lt)) * 0.6931471805599453f : -INFINITY;
