@@ -56,6 +56,15 @@ def test_projection_write_many_tiles_per_cta(pool):
     _check_projection("torch", torch.bfloat16, pool, (512, 8, 16), [7000, 9000, 4100])
 
 
+@pytest.mark.parametrize("pool", ["i8_f16scale", "f16"])
+@pytest.mark.parametrize("t_per_seq", [[30, 34], [1, 5, 2], [120, 80, 55]])
+def test_projection_write_small_batch_cluster_split(pool, t_per_seq):
+    """Decode-sized batches: few 128-token tiles, so d_model is split across the
+    CTAs of a cluster (eight here: 8 heads, d_model 1024) and the partial tiles
+    are summed through distributed shared memory before the epilogue."""
+    _check_projection("torch", torch.bfloat16, pool, (1024, 8, 16), t_per_seq)
+
+
 def _check_projection(backend, dtype, pool, shape, t_per_seq):
     from pie_b200 import ops
     from pie_b200.workloads import empty_head_major_scales
