@@ -499,13 +499,15 @@ class ProjectWriteWorkload(Workload):
 
     ROWS = 64  # tokens per CPU unit
 
-    def __init__(self, seed: int, device, cpu_only: bool = False):
+    def __init__(self, seed: int, device, cpu_only: bool = False, tokens: int = 0):
         from pie_b200.workloads import CONFIGS, block_tables, draw_context_lengths
 
         self.name = "project_write_int8"
         cfg = CONFIGS["prefill_bf16"]
         gen = torch.Generator().manual_seed(seed)
         L = draw_context_lengths(gen, cfg["B"], *cfg["ctx_range"])
+        if tokens:  # one sequence of `tokens` new tokens (a decode-sized batch)
+            L = [tokens]
         Hq, Hkv, D, BS = cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["BS"]
         dm = Hq * D
         bt, nblk, NB = block_tables(gen, L, BS)
@@ -523,7 +525,8 @@ class ProjectWriteWorkload(Workload):
                      "kv_dtype": "int8", "scales": "fp16 per (token, head), head-major"}
         self.unit, self.scale, self.bound, self.dtype = "TFLOP/s", 1e-12, "tensor", "bf16"
         self.metric = ("K/V projection with the INT8 paged-cache write in its epilogue, TFLOP/s "
-                       "(T = prefill_bf16 tokens, d_model 4096, 8 KV heads, D=128)")
+                       f"(T = {'%d tokens' % tokens if tokens else 'prefill_bf16 tokens'}, d_model 4096, 8 KV heads, "
+                       "D=128)")
         self.kernel = "kv_project_write (kv_project_kernel)"
         self.dominant_name = "kv_project_kernel"
         self.launches = 1
@@ -671,13 +674,13 @@ class LongCtxWorkload(Workload):
 
 
 def make_workload(name: str, ws: int, rank: int, device, cpu_only: bool = False, exchange: str = "nccl",
-                  batch: int = 0) -> Workload:
+                  batch: int = 0, tokens: int = 0) -> Workload:
     if name in ("prefill_bf16", "prefill_int8"):
         return PrefillWorkload(1000 + rank, device, cpu_only, int8=name == "prefill_int8")
     if name == "long_ctx_int8":
         return LongCtxWorkload(ws, rank, device, cpu_only, exchange, batch)
     if name == "project_write_int8":
-        return ProjectWriteWorkload(1000 + rank, device, cpu_only)
+        return ProjectWriteWorkload(1000 + rank, device, cpu_only, tokens)
     return DecodeWorkload(name, 1000 + rank, device, cpu_only)
 
 
@@ -918,6 +921,9 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="long_ctx_int8 with fewer sequences (same context-length draws), for small profiler "
                          "captures; 0 = the workload's 256")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="project_write_int8 with one sequence of this many tokens (a decode-sized batch); "
+                         "0 = the prefill_bf16 tokens")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
 
@@ -931,7 +937,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     peaks, peak_kind = load_peaks()
-    w = make_workload(a.workload, ws, rank, device, exchange=a.exchange, batch=a.batch)
+    w = make_workload(a.workload, ws, rank, device, exchange=a.exchange, batch=a.batch, tokens=a.tokens)
     rec = measure(w, a, device, ws, rank, local, peaks, peak_kind, not a.no_cpu_baseline)
     close = getattr(w, "close", None)
     if close is not None:
