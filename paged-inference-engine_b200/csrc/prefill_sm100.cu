@@ -530,7 +530,13 @@ constexpr int P2_V = P2_K + P2_KS * TILE_B;
 constexpr int P2_BAR = P2_V + P2_VS * TILE_B;     // 224 KB
 enum : int { C_QFULL = 0, C_QREADY = 1, C_KFULL = 2, C_KEMPTY = 5, C_VFULL = 8, C_VEMPTY = 10, C_SFULL = 12,
              C_PFULL = 14, C_ODONE = 16, C_TMEMSLOT = 18, C_QEMPTY = 19, C_IFULL = 20, C_IEMPTY = 22,
-             C_RING = 24 };  // C_RING: two 16-byte work-item slots, bytes 192..223 of the barrier area
+             C_RING = 24,  // two 16-byte work-item slots, bytes 192..223 of the barrier area
+             C_QFULL_B = 28, C_QREADY_B = 29, C_QEMPTY_B = 30 };
+// Q barriers per head: head a uses C_QFULL / C_QREADY / C_QEMPTY, head b the _B slots, so head a's
+// next Q tile loads as soon as head a's last Q*K^T has read its buffer.
+__device__ __forceinline__ constexpr int q_full(int x) { return x ? C_QFULL_B : C_QFULL; }
+__device__ __forceinline__ constexpr int q_ready(int x) { return x ? C_QREADY_B : C_QREADY; }
+__device__ __forceinline__ constexpr int q_empty(int x) { return x ? C_QEMPTY_B : C_QEMPTY; }
 
 // PA_PF_ROW1 = 0 (default): two softmax threads per query row, each taking
 // 64 keys of every tile (16 softmax warps, 96 registers a thread), the row
@@ -585,9 +591,11 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
   volatile int* ring = reinterpret_cast<volatile int*>(sm + P2_BAR + 8 * C_RING);  // [2][item, qlen, nkeys, off]
 
   if (tid == 0) {
-    mbar_init(bar(C_QFULL), 1);
-    mbar_init(bar(C_QREADY), 32 * P2_SOFTMAX_WARPS);
-    mbar_init(bar(C_QEMPTY), 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar(q_full(x)), 1);
+      mbar_init(bar(q_ready(x)), 16 * P2_SOFTMAX_WARPS);  // the head's softmax threads
+      mbar_init(bar(q_empty(x)), 1);
+    }
     for (int s = 0; s < P2_KS; ++s) {
       mbar_init(bar(C_KFULL + s), 1);
       mbar_init(bar(C_KEMPTY + s), 1);
@@ -667,16 +675,17 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
       const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
       if (nt > 0) {
         if (lane == 0) {
-          if (qi > 0) wait_or_flag(p, bar(C_QEMPTY), (qi - 1) & 1);  // the last item's Q*K^T have read Q
-          mbar_arrive_expect_tx(bar(C_QFULL), 2 * TILE_B);
           // Q tile: rows m0.. of sequence b (ragged rows: rows q_start[b] + m0.. of the packed Q; rows past
           // its end read as zeros and rows of the next sequence are computed but never stored)
           const int q_row0 = p.q_start ? p.q_start[b] + m0 : m0;
           const int q_seq = p.q_start ? 0 : b;
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(C_QFULL), 0, q_row0, hq0 + x, q_seq);
-            tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(C_QFULL), 64, q_row0, hq0 + x, q_seq);
+            // head x's buffer is free once the last item's Q*K^T of head x have read it
+            if (qi > 0) wait_or_flag(p, bar(q_empty(x)), (qi - 1) & 1);
+            mbar_arrive_expect_tx(bar(q_full(x)), TILE_B);
+            tma_load_4d(base + (x ? P2_QB : P2_QA), &maps.q, bar(q_full(x)), 0, q_row0, hq0 + x, q_seq);
+            tma_load_4d(base + (x ? P2_QB : P2_QA) + HALF_B, &maps.q, bar(q_full(x)), 64, q_row0, hq0 + x, q_seq);
           }
         }
         const int boxs = p.BS < 16 ? p.BS : 16;
@@ -758,14 +767,15 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         const int kend = min(nkeys, off + m0 + TC_BM);
         const int nt = kend > 0 ? (kend + TC_BN - 1) / TC_BN : 0;
         if (nt == 0) continue;
-        if constexpr (Q_CONVERT) wait_or_flag(p, bar(C_QREADY), qi & 1);
-        else wait_or_flag(p, bar(C_QFULL), qi & 1);
         wait_or_flag(p, bar(C_KFULL + gt % P2_KS), (gt / P2_KS) & 1);
-        tc_fence_after();
-        qk(0, 0);
-        qk(1, 0);
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {  // each head as soon as its own Q tile is ready
+          wait_or_flag(p, bar(Q_CONVERT ? q_ready(x) : q_full(x)), qi & 1);
+          tc_fence_after();
+          qk(x, 0);
+          if (nt == 1) tc_commit(bar(q_empty(x)));  // head x's Q is free once this product is done
+        }
         tc_commit(bar(C_KEMPTY + gt % P2_KS));
-        if (nt == 1) tc_commit(bar(C_QEMPTY));  // Q is free once these products are done
         for (int j = 0; j < nt; ++j) {
           const int g = gt + j;
           wait_or_flag(p, bar(C_VFULL + g % P2_VS), (g / P2_VS) & 1);
@@ -775,13 +785,14 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
             wait_or_flag(p, bar(C_KFULL + (g + 1) % P2_KS), ((g + 1) / P2_KS) & 1);
             tc_fence_after();
             qk(0, j + 1);
+            if (j + 2 == nt) tc_commit(bar(q_empty(0)));
           }
           pv(1, j);
           tc_commit(bar(C_VEMPTY + g % P2_VS));
           if (more) {
             qk(1, j + 1);
             tc_commit(bar(C_KEMPTY + (g + 1) % P2_KS));
-            if (j + 2 == nt) tc_commit(bar(C_QEMPTY));
+            if (j + 2 == nt) tc_commit(bar(q_empty(1)));
           }
         }
         gt += nt;
@@ -809,7 +820,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     // waits for the Q tile itself).  A next item's Q is converted before the
     // current item's epilogue, so its first Q*K^T overlaps that epilogue.
     auto convert_q = [&](int q_phase) {
-      wait_or_flag(p, bar(C_QFULL), q_phase & 1);
+      wait_or_flag(p, bar(q_full(x)), q_phase & 1);
       uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
 #pragma unroll 4
       for (int i = r; i < TILE_B / 16; i += 128) {
@@ -821,7 +832,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         q4[i] = v;
       }
       fence_proxy_async_smem();
-      mbar_arrive(bar(C_QREADY));
+      mbar_arrive(bar(q_ready(x)));
     };
     int gt = 0, qi = 0;
     int item, qlen, nkeys, off;
@@ -1027,7 +1038,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
     // current item's epilogue, so its first Q*K^T overlaps that epilogue
     // (measured: 721-737 TFLOP/s against 695-704 converting after it).
     auto convert_q = [&](int q_phase) {
-      wait_or_flag(p, bar(C_QFULL), q_phase & 1);
+      wait_or_flag(p, bar(q_full(x)), q_phase & 1);
       uint4* q4 = reinterpret_cast<uint4*>(sm + (x ? P2_QB : P2_QA));
 #pragma unroll 4
       for (int i = hf * 128 + r; i < TILE_B / 16; i += 256) {
@@ -1039,7 +1050,7 @@ __global__ void __launch_bounds__(P2_THREADS, 1)
         q4[i] = v;
       }
       fence_proxy_async_smem();
-      mbar_arrive(bar(C_QREADY));
+      mbar_arrive(bar(q_ready(x)));
     };
     int gt = 0, qi = 0;
     int item, qlen, nkeys, off;
