@@ -39,8 +39,11 @@ def _worker(rank, world, port, result_path, fail_rank, q_len=1):
     for p in (ROOT, PKG):
         if p not in sys.path:
             sys.path.insert(0, p)
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    torch.distributed.init_process_group("gloo", rank=rank, world_size=world,
+    # Rendezvous through a store with a generous wait (spawned ranks import torch at their own pace); the
+    # process group's own 10 s limit then bounds the collectives, so a rank that never joins one ends the
+    # other ranks' wait quickly.
+    store = torch.distributed.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=120))
+    torch.distributed.init_process_group("gloo", store=store, rank=rank, world_size=world,
                                          timeout=datetime.timedelta(seconds=10))
     from pie_b200.sharded import KVHeadShardedDecoder
     from pie_b200.workloads import make_decode_batch
