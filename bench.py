@@ -3,7 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload long_ctx_int8|decode_fp16|decode_int8|prefill_bf16|prefill_int8|
                                 project_write_int8]
-                    [--exchange nccl|peer] [--no-extra] [--no-cpu-baseline]
+                    [--exchange nccl|peer] [--no-extra] [--no-cpu-baseline] [--no-reference-kernel]
+                    [--batch B (long_ctx_int8)] [--tokens T (project_write_int8)]
 
 One step = one pass of the hot path over one batch of seeded synthetic input
 with the reference's benchmark shapes (no public dataset is involved):
